@@ -1,0 +1,155 @@
+/*
+ * qgemm_b200.h -- C-ABI of the B200 (sm_100a) weight-only 4-bit GEMM path.
+ *
+ *   Y[M,N] = X[M,K] . W[N,K]^T      X bf16 row-major, W packed 4-bit along K,
+ *                                    FP32 accumulation, Y bf16 (or fp32).
+ *
+ * The byte layouts are exactly those of titoatwork/qgemm-mx
+ * include/qgemm/pack.hpp:14-85 (nibble 2i low / 2i+1 high, row-major linear
+ * index n*K+k; scales in a separate array indexed n*(K/block)+k/block):
+ *   MXFP4      E2M1 elements + one E8M0 byte per 32 along K
+ *   NVFP4      E2M1 elements + one E4M3 byte per 16 along K + FP32 tensor scale
+ *   INT4_G128  symmetric two's-complement nibbles + FP16 scale bits per 128
+ *   INT4_G64   same, group 64
+ * The reference exposes this path only as header-only C++ (no C-ABI); each
+ * entry point below names the reference symbol whose behaviour it carries.
+ *
+ * Conventions
+ *   - All data pointers are DEVICE pointers unless a parameter says otherwise;
+ *     the caller owns every buffer.  Nothing here allocates device memory
+ *     inside a GEMM call, synchronises, or reads back to the host, so every
+ *     call is stream-ordered and can be captured into a CUDA graph (the
+ *     reference's time_graphed protocol, timing.cuh:288-336).
+ *   - `stream` is a cudaStream_t passed as void*.
+ *   - Errors come back as qgemm_status_t; nothing throws or exits across the
+ *     ABI.  Conditions on which the reference throws std::invalid_argument
+ *     (pack.hpp:115,122,427-430,467,505-508) return QGEMM_ERR_INVALID_ARG.
+ *     qgemm_last_error_message() gives the text for the calling thread.
+ */
+#ifndef QGEMM_B200_H
+#define QGEMM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  QGEMM_OK = 0,
+  QGEMM_ERR_INVALID_ARG = 1,      /* bad pointer/size/format (reference: throw) */
+  QGEMM_ERR_UNSUPPORTED_SHAPE = 2,/* shape the kernels do not cover            */
+  QGEMM_ERR_CUDA = 3,             /* a CUDA runtime call or launch failed      */
+  QGEMM_ERR_NCCL = 4,             /* an NCCL call failed                       */
+  QGEMM_ERR_TIMEOUT = 5,          /* a bounded device-side wait gave up        */
+  QGEMM_ERR_WORKSPACE = 6         /* workspace missing or too small            */
+} qgemm_status_t;
+
+/* Mirrors qgemm::Format (formats.cuh:16-24) for the 4-bit members; the dense
+ * entries exist only for byte accounting. */
+typedef enum {
+  QGEMM_FMT_MXFP4 = 0,
+  QGEMM_FMT_NVFP4 = 1,
+  QGEMM_FMT_INT4_G128 = 2,
+  QGEMM_FMT_INT4_G64 = 3,
+  QGEMM_FMT_BF16 = 4,      /* accounting only */
+  QGEMM_FMT_FP16 = 5,      /* accounting only */
+  QGEMM_FMT_FP8_E4M3 = 6   /* accounting only */
+} qgemm_format_t;
+
+/* A packed weight matrix resident in device memory.  Replaces the reference's
+ * PackedMxfp4 / PackedNvfp4 / PackedInt4 containers (pack.hpp:396-417), whose
+ * std::vector members become device pointers of the same length and layout. */
+typedef struct {
+  int32_t format;          /* qgemm_format_t (4-bit members only)           */
+  int32_t reserved;        /* must be 0                                      */
+  size_t N, K;             /* W is [N, K]                                    */
+  const uint8_t* data;     /* N*K/2 bytes                                    */
+  const void* scales;      /* MXFP4/NVFP4: uint8 [N*K/blk]; INT4: uint16 bits */
+  float tensor_scale;      /* NVFP4 per-tensor FP32 scale; ignored otherwise */
+} qgemm_weights_t;
+
+/* ---- library -------------------------------------------------------------- */
+const char* qgemm_version(void);
+const char* qgemm_status_string(qgemm_status_t s);
+/* Message of the last failing call made by this host thread ("" if none). */
+const char* qgemm_last_error_message(void);
+
+/* ---- byte accounting: formats.cuh:40-109 ---------------------------------- */
+double qgemm_bytes_per_weight(int32_t format);                   /* formats.cuh:67-69 */
+size_t qgemm_weight_bytes(int32_t format, size_t N, size_t K);   /* formats.cuh:73-76 */
+size_t qgemm_total_bytes(int32_t format, size_t M, size_t N, size_t K); /* :80-83 */
+double qgemm_flops(size_t M, size_t N, size_t K);                /* formats.cuh:91-94 */
+/* Exact buffer sizes of a packed matrix (pack.hpp:113-153). */
+qgemm_status_t qgemm_packed_sizes(int32_t format, size_t N, size_t K,
+                                  size_t* data_bytes, size_t* scale_bytes);
+
+/* ---- packers: device quantize + pack, bit-exact to pack.hpp -------------- *
+ * W is FP32 row-major [N,K] on the device.  Outputs use the reference layout.
+ * Each returns QGEMM_ERR_INVALID_ARG on the reference's throw conditions.    */
+/* pack.hpp:465-497 pack_mxfp4 */
+qgemm_status_t qgemm_pack_mxfp4(const float* W, size_t N, size_t K,
+                                uint8_t* data, uint8_t* scales, void* stream);
+/* pack.hpp:502-542 pack_nvfp4 (tensor_scale: finite, > 0, host value) */
+qgemm_status_t qgemm_pack_nvfp4(const float* W, size_t N, size_t K,
+                                float tensor_scale, uint8_t* data,
+                                uint8_t* scales, void* stream);
+/* pack.hpp:424-462 pack_int4 (group 64 or 128; scales = FP16 bits) */
+qgemm_status_t qgemm_pack_int4(const float* W, size_t N, size_t K, int32_t group,
+                               uint8_t* data, uint16_t* scales, void* stream);
+/* NVFP4 per-tensor scale max|W|/(448*6) into *out (device float).  The
+ * reference takes this value as a caller argument (pack.hpp:502-508). */
+qgemm_status_t qgemm_nvfp4_tensor_scale(const float* W, size_t n, float* out,
+                                        void* stream);
+
+/* ---- dequant: pack.hpp:548-585 dequant_{int4,mxfp4,nvfp4}, bit-exact ------ */
+qgemm_status_t qgemm_dequant(const qgemm_weights_t* w, float* out, void* stream);
+
+/* ---- scalar codecs on the device, bit-exact to pack.hpp:183-374 ----------- *
+ * kind: 0 e2m1_encode -> uint8, 1 e8m0_encode -> uint8, 2 e4m3_encode -> uint8,
+ *       3 float_to_fp16_bits -> uint16.                                      */
+qgemm_status_t qgemm_codec_encode(int32_t kind, const float* in, void* out,
+                                  size_t n, void* stream);
+
+/* ---- GEMM ------------------------------------------------------------------
+ * Workspace: scratch the kernels use for split-K partial sums and tile
+ * counters.  Size it with qgemm_workspace_size(); zero it once before first
+ * use (qgemm_workspace_init or cudaMemsetAsync).  Every call leaves it zeroed
+ * again.  Calls that may overlap on the GPU need distinct workspaces.        */
+size_t qgemm_workspace_size(const qgemm_weights_t* w, int32_t M);
+qgemm_status_t qgemm_workspace_init(void* workspace, size_t ws_bytes, void* stream);
+
+/* Y = X . W^T.  X: bf16 bits [M,K]; Y: bf16 bits [M,N].  Any M >= 1.
+ * Result is within the reference GEMM (ref_gemm.hpp:15-27, double
+ * accumulation) by max-abs <= 1e-2*||row||_inf and rel-Frobenius <= 1e-3. */
+qgemm_status_t qgemm_gemm_w4a16(const qgemm_weights_t* w, const uint16_t* X,
+                                int32_t M, uint16_t* Y, void* workspace,
+                                size_t ws_bytes, void* stream);
+/* Same, FP32 output (no final bf16 rounding). */
+qgemm_status_t qgemm_gemm_w4a16_f32(const qgemm_weights_t* w, const uint16_t* X,
+                                    int32_t M, float* Y, void* workspace,
+                                    size_t ws_bytes, void* stream);
+
+/* ---- baselines and probes (bench harness; not on the product path) ------- */
+/* cuBLAS BF16 dense Y[M,N] = X[M,K] . W[N,K]^T (bench_cublas.cu:144-151 with
+ * CUDA_R_16BF in place of CUDA_R_16F, COMPUTE_32F). */
+qgemm_status_t qgemm_cublas_bf16_gemm(const uint16_t* W, const uint16_t* X,
+                                      int32_t M, size_t N, size_t K, uint16_t* Y,
+                                      void* stream);
+/* Memory probes (bandwidth.cu:25-50, bench_stream_ideal.cu:29-39).
+ * kind: 0 read-only with 128-bit loads, 1 read-only with TMA bulk copies
+ * (cp.async.bulk, no multicast), 2 copy src->dst, 3 write-only fill dst.
+ * bytes must be a multiple of 16; src/dst 16-byte aligned.                   */
+qgemm_status_t qgemm_probe_launch(int32_t kind, const void* src, void* dst,
+                                  size_t bytes, void* stream);
+/* Synchronous: reports (and returns QGEMM_ERR_TIMEOUT) if a bounded wait in
+ * a TMA bulk probe gave up on this device.  Not capturable. */
+qgemm_status_t qgemm_probe_status(int32_t* timed_out);
+/* SM count and L2 bytes of the current device (timing.cuh:50-91). */
+qgemm_status_t qgemm_device_info(int32_t* sm_count, size_t* l2_bytes);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QGEMM_B200_H */

@@ -1,0 +1,196 @@
+// probe.cu -- memory-bandwidth probes and the cuBLAS BF16 dense baseline.
+//
+// The probes re-target titoatwork/qgemm-mx src/probe/bandwidth.cu:25-50 and
+// src/bench/bench_stream_ideal.cu:29-39 to B200: the read-only probe that
+// gives the project's HBM denominator exists in two forms, 128-bit vector
+// loads (grid-stride, sized in multiples of the SM count) and TMA bulk copies
+// (cp.async.bulk global->shared, completion on an mbarrier, no multicast).
+// Every mbarrier wait is bounded by %globaltimer; a timeout sets a device
+// flag that qgemm_probe_launch reports on the next call instead of hanging.
+#include <cublas_v2.h>
+
+#include "common.cuh"
+
+namespace qg {
+
+__device__ unsigned g_probe_timeout = 0;
+__device__ unsigned g_probe_sink = 0;
+
+__global__ void k_read16(const uint4* __restrict__ in, size_t n4) {
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  uint32_t acc = 0;
+  size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; i + 3 * stride < n4; i += 4 * stride) {  // 4 independent loads in flight
+    uint4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(v[u].x), "=r"(v[u].y), "=r"(v[u].z), "=r"(v[u].w)
+                   : "l"(in + i + u * stride));
+#pragma unroll
+    for (int u = 0; u < 4; ++u) acc ^= v[u].x ^ v[u].y ^ v[u].z ^ v[u].w;
+  }
+  for (; i < n4; i += stride) {
+    const uint4 v = in[i];
+    acc ^= v.x ^ v.y ^ v.z ^ v.w;
+  }
+  if (acc == 0x9E3779B9u) g_probe_sink = acc;  // keeps the loads alive
+}
+
+__global__ void k_copy16(const uint4* __restrict__ in, uint4* __restrict__ out, size_t n4) {
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) out[i] = in[i];
+}
+
+__global__ void k_write16(uint4* __restrict__ out, size_t n4) {
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  const uint4 v = make_uint4(1u, 2u, 3u, 4u);
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) out[i] = v;
+}
+
+// ---- TMA bulk read -----------------------------------------------------------
+constexpr int kBulkStages = 6;
+constexpr int kBulkBytes = 16384;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+// Wait for the phase with the given parity; false after ~limit_ns.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned long long limit_ns) {
+  const unsigned long long t0 = globaltimer();
+  for (;;) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    if (ok) return true;
+    if (globaltimer() - t0 > limit_ns) return false;
+  }
+}
+
+__global__ void __launch_bounds__(32) k_read_bulk(const uint8_t* __restrict__ in, size_t nchunks) {
+  extern __shared__ __align__(128) uint8_t sm[];
+  __shared__ __align__(8) unsigned long long bars[kBulkStages];
+  if (threadIdx.x != 0) return;
+  for (int s = 0; s < kBulkStages; ++s)
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&bars[s])));
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  const size_t first = blockIdx.x, step = gridDim.x;
+  auto issue = [&](size_t chunk, int s) {
+    const uint32_t bar = smem_u32(&bars[s]);
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(kBulkBytes) : "memory");
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(sm + (size_t)s * kBulkBytes)),
+        "l"(in + chunk * kBulkBytes), "r"(kBulkBytes), "r"(bar)
+        : "memory");
+  };
+  int s = 0;
+  size_t c = first;
+  for (int k = 0; k < kBulkStages && c < nchunks; ++k, c += step) issue(c, k);
+  uint32_t phase[kBulkStages] = {0, 0, 0, 0, 0, 0};
+  for (size_t done = first; done < nchunks; done += step) {
+    if (!mbar_wait(smem_u32(&bars[s]), phase[s], 200000000ull)) {  // 200 ms
+      atomicExch(&g_probe_timeout, 1u);
+      // drain: give the copies still in flight a bounded chance to land
+      for (int k = 0; k < kBulkStages; ++k) (void)mbar_wait(smem_u32(&bars[k]), phase[k], 50000000ull);
+      return;
+    }
+    phase[s] ^= 1u;
+    if (c < nchunks) { issue(c, s); c += step; }
+    s = (s + 1) % kBulkStages;
+  }
+}
+
+static cublasHandle_t cublas_handle() {
+  static thread_local cublasHandle_t h[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!h[dev]) {
+    if (cublasCreate(&h[dev]) != CUBLAS_STATUS_SUCCESS) h[dev] = nullptr;
+  }
+  return h[dev];
+}
+
+}  // namespace qg
+
+using namespace qg;
+
+extern "C" {
+
+qgemm_status_t qgemm_device_info(int32_t* sm_count, size_t* l2_bytes) {
+  DevProps p;
+  qgemm_status_t st = device_props(&p);
+  if (st != QGEMM_OK) return st;
+  if (sm_count) *sm_count = p.sm_count;
+  if (l2_bytes) *l2_bytes = p.l2_bytes;
+  return QGEMM_OK;
+}
+
+qgemm_status_t qgemm_probe_launch(int32_t kind, const void* src, void* dst, size_t bytes, void* stream) {
+  if (bytes % 16 != 0) return fail(QGEMM_ERR_INVALID_ARG, "probe: bytes must be a multiple of 16");
+  if (kind < 0 || kind > 3) return fail(QGEMM_ERR_INVALID_ARG, "probe: unknown kind %d", (int)kind);
+  if ((kind != 3 && (!src || (reinterpret_cast<uintptr_t>(src) & 15u))) ||
+      (kind >= 2 && (!dst || (reinterpret_cast<uintptr_t>(dst) & 15u))))
+    return fail(QGEMM_ERR_INVALID_ARG, "probe: null or misaligned buffer");
+  DevProps p;
+  qgemm_status_t st = device_props(&p);
+  if (st != QGEMM_OK) return st;
+  cudaStream_t s = as_stream(stream);
+  const size_t n4 = bytes / 16;
+  const unsigned grid = (unsigned)p.sm_count * 4;
+  switch (kind) {
+    case 0: k_read16<<<grid, 512, 0, s>>>(static_cast<const uint4*>(src), n4); break;
+    case 1: {
+      if (bytes % kBulkBytes != 0)
+        return fail(QGEMM_ERR_INVALID_ARG, "probe: TMA bulk probe needs a multiple of %d bytes", kBulkBytes);
+      const size_t smem = (size_t)kBulkStages * kBulkBytes;
+      static bool attr[64] = {false};
+      int dev = 0;
+      QG_CUDA_RET(cudaGetDevice(&dev));
+      if (dev < 0 || dev >= 64) return fail(QGEMM_ERR_CUDA, "probe: device ordinal %d out of range", dev);
+      if (!attr[dev]) {
+        QG_CUDA_RET(cudaFuncSetAttribute(k_read_bulk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        attr[dev] = true;
+      }
+      k_read_bulk<<<(unsigned)p.sm_count * 2, 32, smem, s>>>(static_cast<const uint8_t*>(src), bytes / kBulkBytes);
+      break;
+    }
+    case 2: k_copy16<<<grid, 512, 0, s>>>(static_cast<const uint4*>(src), static_cast<uint4*>(dst), n4); break;
+    default: k_write16<<<grid, 512, 0, s>>>(static_cast<uint4*>(dst), n4); break;
+  }
+  QG_LAUNCH_RET();
+  return QGEMM_OK;
+}
+
+qgemm_status_t qgemm_probe_status(int32_t* timed_out) {
+  unsigned flag = 0;
+  QG_CUDA_RET(cudaMemcpyFromSymbol(&flag, g_probe_timeout, sizeof(flag)));
+  if (timed_out) *timed_out = (int32_t)flag;
+  return flag ? fail(QGEMM_ERR_TIMEOUT, "probe: a TMA bulk probe wait timed out") : QGEMM_OK;
+}
+
+qgemm_status_t qgemm_cublas_bf16_gemm(const uint16_t* W, const uint16_t* X, int32_t M, size_t N, size_t K,
+                                      uint16_t* Y, void* stream) {
+  if (!W || !X || !Y || M < 1 || N == 0 || K == 0)
+    return fail(QGEMM_ERR_INVALID_ARG, "cublas_bf16_gemm: bad arguments");
+  cublasHandle_t h = cublas_handle();
+  if (!h) return fail(QGEMM_ERR_CUDA, "cublas_bf16_gemm: cublasCreate failed");
+  if (cublasSetStream(h, as_stream(stream)) != CUBLAS_STATUS_SUCCESS)
+    return fail(QGEMM_ERR_CUDA, "cublas_bf16_gemm: cublasSetStream failed");
+  const float alpha = 1.0f, beta = 0.0f;
+  // Y_rm[M,N] = X_rm[M,K] . W_rm[N,K]^T  ==  C_cm[N,M] = op_T(W_cm[K,N]) . X_cm[K,M]
+  const cublasStatus_t cs = cublasGemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, (int)N, (int)M, (int)K, &alpha, W,
+                                         CUDA_R_16BF, (int)K, X, CUDA_R_16BF, (int)K, &beta, Y, CUDA_R_16BF,
+                                         (int)N, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+  if (cs != CUBLAS_STATUS_SUCCESS) return fail(QGEMM_ERR_CUDA, "cublasGemmEx failed (%d)", (int)cs);
+  return QGEMM_OK;
+}
+
+}  // extern "C"

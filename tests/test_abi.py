@@ -1,0 +1,81 @@
+"""The C-ABI library loads without a GPU, exports every entry point declared
+in include/*.h, and its host-only parts behave like the reference: byte
+accounting (formats.cuh), packed sizes (pack.hpp:113-153) and the argument
+checks on which the reference throws (pack.hpp:426-430, 466-468, 504-509)."""
+import ctypes as C
+import glob
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    names = set()
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        src = open(h).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        names |= set(re.findall(r"\b(qgemm_[a-z0-9_]+)\s*\(", src))
+    return sorted(names)
+
+
+def test_header_declares_entry_points():
+    names = declared_symbols()
+    for must in ("qgemm_pack_mxfp4", "qgemm_pack_nvfp4", "qgemm_pack_int4", "qgemm_gemm_w4a16",
+                 "qgemm_dequant", "qgemm_workspace_size"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol(qg):
+    lib = qg.lib()
+    missing = [n for n in declared_symbols() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_byte_accounting_matches_reference_formulas(qg):  # test_formats.cpp:49-117
+    assert qg.bytes_per_weight(qg.MXFP4) == 0.53125
+    assert qg.bytes_per_weight(qg.NVFP4) == 0.5625
+    assert qg.bytes_per_weight(qg.INT4_G128) == 0.515625
+    assert qg.bytes_per_weight(qg.INT4_G64) == 0.53125
+    assert qg.bytes_per_weight(qg.BF16) == 2.0 and qg.bytes_per_weight(qg.FP8_E4M3) == 1.0
+    assert qg.weight_bytes(qg.INT4_G128, 4096, 4096) == 8_650_752
+    assert qg.weight_bytes(qg.MXFP4, 4096, 4096) == 8_912_896
+    assert qg.total_bytes(qg.MXFP4, 1, 4096, 4096) == 8_912_896 + 8192 + 8192
+    assert qg.flops(2, 3, 4) == 48.0
+
+
+def test_accounting_equals_reference_build(qg, ref):
+    for f, rf in [(qg.MXFP4, 0), (qg.NVFP4, 1), (qg.INT4_G128, 2), (qg.INT4_G64, 3)]:
+        for (M, N, K) in [(1, 4096, 4096), (256, 28672, 4096), (7, 2880, 2880), (64, 57344, 8192)]:
+            assert qg.weight_bytes(f, N, K) == ref.lib.ref_weight_bytes(rf, N, K)
+            assert qg.total_bytes(f, M, N, K) == ref.lib.ref_total_bytes(rf, M, N, K)
+
+
+def test_packed_sizes(qg):  # test_formats.cpp:81-106 (N=64, K=256)
+    N, K = 64, 256
+    for f, bpw in [(qg.MXFP4, 0.53125), (qg.NVFP4, 0.5625), (qg.INT4_G128, 0.515625), (qg.INT4_G64, 0.53125)]:
+        d, s = qg.packed_sizes(f, N, K)
+        assert (d + s) / (N * K) == bpw
+    with pytest.raises(ValueError):
+        qg.packed_sizes(qg.MXFP4, 3, 48)
+
+
+def test_argument_checks_return_invalid_arg(qg):
+    """The reference's throw conditions come back as QGEMM_ERR_INVALID_ARG,
+    decided on the host before any device work."""
+    lib = qg.lib()
+    null = C.c_void_p(0)
+    assert lib.qgemm_pack_mxfp4(null, 4, 48, null, null, null) == qg.ERR_INVALID_ARG
+    assert lib.qgemm_pack_nvfp4(null, 4, 40, 1.0, null, null, null) == qg.ERR_INVALID_ARG
+    for ts in (0.0, -2.0, float("inf"), float("nan")):
+        assert lib.qgemm_pack_nvfp4(null, 4, 32, ts, null, null, null) == qg.ERR_INVALID_ARG
+    assert lib.qgemm_pack_int4(null, 4, 128, 32, null, null, null) == qg.ERR_INVALID_ARG
+    assert lib.qgemm_pack_int4(null, 4, 96, 64, null, null, null) == qg.ERR_INVALID_ARG
+    assert b"group" in lib.qgemm_last_error_message() or b"divisible" in lib.qgemm_last_error_message()
+    w = qg._Weights(qg.MXFP4, 0, 64, 256, None, None, 1.0)
+    assert lib.qgemm_gemm_w4a16(C.byref(w), null, 1, null, null, 0, null) == qg.ERR_INVALID_ARG
+    assert lib.qgemm_codec_encode(9, null, null, 4, null) == qg.ERR_INVALID_ARG
+    assert lib.qgemm_probe_launch(0, null, null, 17, null) == qg.ERR_INVALID_ARG
+    assert qg.version().startswith("qgemm-b200")
