@@ -61,7 +61,39 @@ def parse():
     ap.add_argument("--workload", default="llama70b_mxfp4", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--table", action="store_true", help="print the per-(layer, M) table to stderr")
+    ap.add_argument("--case", default=None,
+                    help="fmt,N,K,M: run only that GEMM --steps times (for profilers), print its mean time")
     return ap.parse_args()
+
+
+def run_case(args):
+    """One GEMM configuration launched --warmup + --steps times (eager, one
+    weight buffer); used for ncu captures of a single kernel."""
+    import torch
+    qg = importlib.import_module("qgemm-mx_b200")
+    fmt, N, K, M = args.case.split(",")
+    N, K, M = int(N), int(K), int(M)
+    fcode = {"mxfp4": qg.MXFP4, "nvfp4": qg.NVFP4, "int4": qg.INT4_G128, "int4g64": qg.INT4_G64}[fmt]
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(1)
+    W = torch.randn((N, K), generator=gen, device="cuda").mul_(0.02)
+    p = qg.pack(fcode, W)
+    del W
+    X = torch.randn((M, K), generator=gen, device="cuda").to(torch.bfloat16)
+    Y = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    ws = qg.make_workspace(p, M)
+    for _ in range(args.warmup):
+        qg.gemm_w4a16(p, X, out=Y, workspace=ws)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        qg.gemm_w4a16(p, X, out=Y, workspace=ws)
+    b.record()
+    torch.cuda.synchronize()
+    us = a.elapsed_time(b) * 1e3 / args.steps
+    nb = qg.total_bytes(fcode, M, N, K)
+    print(json.dumps({"case": args.case, "us_per_call": round(us, 3), "gbs": round(nb / us / 1e3, 1)}))
 
 
 def fmt_code(qg, name):
@@ -218,6 +250,9 @@ def run_reference_arm(args):
 
 def main():
     args = parse()
+    if args.case:
+        run_case(args)
+        return
     if args.impl == "reference":
         run_reference_arm(args)
         return

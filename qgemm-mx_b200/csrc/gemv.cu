@@ -1,41 +1,52 @@
-// gemv.cu -- decode-path W4A16 GEMM for small M (M <= 32 per launch).
+// gemv.cu -- decode-path W4A16 GEMM for small M (M <= 16 per launch).
 //
 // Y[M,N] = X[M,K] . W[N,K]^T with W in the reference's packed layouts
-// (titoatwork/qgemm-mx include/qgemm/pack.hpp:14-85) streamed straight from
-// HBM once.  The path is HBM-bound, so the design goals are (1) every weight
-// byte read exactly once with 16-byte coalesced loads, (2) an equal share of
-// the weight stream for every warp on any (N, K), and (3) few ALU
-// instructions per weight.
+// (titoatwork/qgemm-mx include/qgemm/pack.hpp:14-85) streamed from HBM once.
+// The path is HBM-bound; the kernel is built so that (1) every weight byte is
+// read once with coalesced loads, (2) every warp gets an equal share of the
+// weight stream on any (N, K) (stream-K), and (3) dequantisation costs about
+// one instruction per weight, because an instruction-bound kernel cannot keep
+// HBM busy.
 //
-// Math: a swap-AB warp MMA (mma.sync m16n8k16, bf16 in, fp32 accumulate).
-// The 16 weight rows of a tile are the MMA's M side, the (<= 8 per n-tile)
-// activation rows its N side, so tensor cores do the multiply-accumulate and
-// CUDA cores only dequantise.  Dequantisation is exact:
-//   MXFP4  e2m1 * 2^(e8m0-127) is representable in bf16 (<= 2 significant
-//          bits), so the block scale is folded into the bf16 operand;
-//   NVFP4  e2m1 * e4m3 has <= 6 significant bits and lies in [2^-10, 2688],
-//          so the block scale is folded too; the FP32 tensor scale is applied
-//          to the FP32 result;
-//   INT4   q in [-8,7] is exact in bf16; q * fp16-scale is not, so each
-//          group's FP32 partial sum is scaled by the group scale (post-scale).
-// Products of bf16 values are exact in the fp32 accumulator, so Y differs
-// from the double-accumulated reference (ref_gemm.hpp:15-27) only by fp32
-// summation order (and, for NVFP4, by the tensor scale being applied once per
-// output instead of once per weight).
+// Two launches per call, chained with programmatic dependent launch:
+//  k_xprep  X (bf16) -> f16 with a per-row power-of-two prescale 2^-s_m chosen
+//           so that max|x_m| * 2^-s_m lies in [2^14, 2^15).  Every bf16 value
+//           at or above max|x_m| * 2^-29 converts exactly (8 significant bits
+//           fit f16's 11); smaller ones round to f16's subnormal grid, an
+//           error below 2^-39 * max|x_m| per element.  The FP32 epilogue
+//           multiplies by 2^s_m, so no information is lost.
+//  k_gemv   swap-AB warp MMA (mma.sync m16n8k16, f16 in, fp32 accumulate):
+//           16 weight rows are the MMA's M side, <= 8 activation rows per
+//           n-tile its N side.  W codes are widened by the hardware
+//           cvt.rn.f16x2.e2m1x2 (sign included) or, for INT4, by an f16
+//           magic-number conversion; all dequantised values are exact.
+//             MXFP4  the E8M0 block scale is applied to the FP32 partial sum of
+//                    each 32-block (post-scale): the K-slot mapping puts one
+//                    block in each pair of MMAs.
+//             NVFP4  e2m1*e4m3 has <= 6 significant bits within [2^-10, 2688]
+//                    and is exact in f16: the block scale is folded into the
+//                    operand with one f16x2 multiply; the FP32 tensor scale is
+//                    applied in the epilogue.
+//             INT4   q in [-8,7] is exact in f16; each 64/128-group's FP32
+//                    partial sum is scaled by its FP16 scale.
+//           Products are exact in the FP32 accumulator, so Y differs from the
+//           double-accumulated reference (ref_gemm.hpp:15-27) only by FP32
+//           summation order and the tensor scale applied once per output.
 //
-// K-slot mapping: an MMA reduces over 16 "k slots"; lane (g = lane/4,
+// K-slot mapping: an m16n8k16 MMA reduces over 16 k slots; lane (g = lane/4,
 // j = lane%4) owns slots {2j, 2j+1, 2j+8, 2j+9}.  Any bijection between slots
-// and true k works as long as the weight (A) and activation (B) fragments use
-// the same one, so each lane loads one contiguous 16-byte run of packed codes
-// (32 k) per weight row and the matching 64-byte run of X: no shuffles.
+// and true k works if the weight (A) and activation (B) fragments agree, so
+// lanes load contiguous runs of packed codes and k_xprep writes X in the
+// matching order.
 //
-// Schedule: stream-K.  The iteration space (row tile, 128-k chunk) is cut
-// into one contiguous range per warp.  A tile finished inside one warp is
-// stored directly; a tile split across warps leaves FP32 partial fragments in
-// the workspace, and the warp whose atomic ticket shows it arrived last sums
-// all contributors' partials in warp order (deterministic) and stores Y.
-// Nobody waits on anybody: there is no spin loop in this kernel.
+// Schedule: stream-K.  The iteration space (tile of 32 weight rows, 128-k
+// chunk) is cut into one contiguous range per warp.  A tile finished inside
+// one warp is stored directly; a tile split across warps leaves FP32 partial
+// fragments in the workspace, and the warp whose atomic ticket shows it
+// arrived last sums all contributors' partials in warp order (deterministic)
+// and stores Y.  There is no spin-wait anywhere in this file.
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "common.cuh"
 
@@ -43,121 +54,216 @@ namespace qg {
 
 constexpr int kWarpsPerCta = 4;
 constexpr int kChunkK = 128;
+constexpr int kRowTiles = 2;          // 16-row MMA tiles per warp tile
+constexpr int kTileRows = 16 * kRowTiles;
+constexpr int kMaxM = 16;             // activation rows per launch
 
 struct GemvArgs {
   const uint8_t* data;
   const void* scales;
-  const uint16_t* X;
+  const __half* Xh;     // [mpad, K] f16, prescaled (and permuted for INT4)
+  const float* xs;      // [mpad] 2^s_m
   void* Y;
-  int M, N, K;
+  int M, N, K, ldy;
   float ts;
-  float* partials;      // [2 * W_total][R*NT*32*4] floats
+  float* partials;      // [2 * W_total][slot]
   unsigned* counters;   // [tiles]
   long long T;          // iterations = tiles * C
   int C;                // chunks per tile
   int W_total;          // warps that own iterations
 };
 
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t s) {
-  uint32_t d;
-  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(s));
-  return d;
-}
-__device__ __forceinline__ uint32_t lop_or_and(uint32_t a, uint32_t b, uint32_t m) {
-  // a | (b & m)
-  uint32_t d;
-  asm("lop3.b32 %0, %1, %2, %3, 0xF8;" : "=r"(d) : "r"(a), "r"(b), "r"(m));
-  return d;
-}
-__device__ __forceinline__ uint32_t hmul2_bf16(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-__device__ __forceinline__ uint32_t hsub2_bf16(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
+// ---------------------------------------------------------------------------
+// small PTX helpers
+// ---------------------------------------------------------------------------
 
-__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                         uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-      "{%8,%9}, {%0,%1,%2,%3};"
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
+// d = A.B (accumulator starts at zero)
+__device__ __forceinline__ void mma_f16_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+  const float z = 0.0f;
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
+}
 
-// 16-byte streaming load of packed weights: read once, keep out of L1.
-__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+__device__ __forceinline__ uint4 ldg_stream16(const void* p) {  // read once: skip L1
   uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
+  asm("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
   return v;
 }
 __device__ __forceinline__ uint2 ldg_stream8(const void* p) {
   uint2 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+  asm("ld.global.nc.L1::no_allocate.L2::256B.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
   return v;
 }
-// Activations: re-read by every warp, keep cached.
-__device__ __forceinline__ uint4 ldg_keep(const void* p) {
-  return __ldg(reinterpret_cast<const uint4*>(p));
+// 4-byte pieces of one 16-byte block: allocate in L1 so the 3 sibling loads
+// of the same sector hit there.
+__device__ __forceinline__ uint32_t ldg_first4(const void* p) {
+  uint32_t v;
+  asm("ld.global.nc.L1::evict_first.L2::256B.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint4 ldg_keep16(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+
+// byte t of q (codes 2t, 2t+1) -> f16x2 (low half = even code)
+__device__ __forceinline__ void e2m1x8_to_f16(uint32_t q, uint32_t (&o)[4]) {
+  asm("{ .reg .b8 b0, b1, b2, b3;\n"
+      "  mov.b32 {b0, b1, b2, b3}, %4;\n"
+      "  cvt.rn.f16x2.e2m1x2 %0, b0;\n"
+      "  cvt.rn.f16x2.e2m1x2 %1, b1;\n"
+      "  cvt.rn.f16x2.e2m1x2 %2, b2;\n"
+      "  cvt.rn.f16x2.e2m1x2 %3, b3; }\n"
+      : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3])
+      : "r"(q));
 }
 
-// 8 E2M1 codes (nibble i = k offset i) -> 4 bf16x2 words (c0,c1) (c2,c3)
-// (c4,c5) (c6,c7), low half = even code.  Magnitudes through a byte-permute
-// lookup of the bf16 bytes of {0,.5,1,1.5,2,3,4,6}; signs by replicating the
-// code's sign bit into the high byte.
-__device__ __forceinline__ void e2m1x8_to_bf16(uint32_t q, uint32_t (&o)[4]) {
-  constexpr uint32_t LO_A = 0xC0800000u, LO_B = 0xC0804000u;  // low bytes
-  constexpr uint32_t HI_A = 0x3F3F3F00u, HI_B = 0x40404040u;  // high bytes
-  const uint32_t s0 = q & 0x7777u, s1 = (q >> 16) & 0x7777u;
-  const uint32_t lo0 = prmt(LO_A, LO_B, s0), lo1 = prmt(LO_A, LO_B, s1);
-  uint32_t hi0 = prmt(HI_A, HI_B, s0), hi1 = prmt(HI_A, HI_B, s1);
-  const uint32_t q4 = q << 4;  // even codes' sign bits become byte msbs
-  hi0 = lop_or_and(hi0, prmt(q4, q, 0xD9C8u), 0x80808080u);
-  hi1 = lop_or_and(hi1, prmt(q4, q, 0xFBEAu), 0x80808080u);
-  o[0] = prmt(lo0, hi0, 0x5140u);
-  o[1] = prmt(lo0, hi0, 0x7362u);
-  o[2] = prmt(lo1, hi1, 0x5140u);
-  o[3] = prmt(lo1, hi1, 0x7362u);
+__device__ __forceinline__ uint32_t hmul2_f16(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
 }
 
-// 8 INT4 codes -> 4 bf16x2 words (c0,c4) (c1,c5) (c2,c6) (c3,c7): the offset
-// nibble u = q+8 is placed in the mantissa of bf16 128.0 and 136 subtracted.
-__device__ __forceinline__ void int4x8_to_bf16(uint32_t q, uint32_t (&o)[4]) {
-  const uint32_t u = q ^ 0x88888888u;
-  constexpr uint32_t MAGIC = 0x43004300u, BIAS = 0x43084308u;  // 128, 136
+// 8 INT4 codes -> f16x2 words (c0,c4) (c1,c5) (c2,c6) (c3,c7).  With
+// u = q ^ 0x8 (= value + 8), nibble u placed in the mantissa of f16 1024
+// gives 1024 + u, or 1024 + 16u when taken from the upper nibble of a byte;
+// one subtract / fused multiply-add recovers the signed value exactly.
+__device__ __forceinline__ void int4x8_to_f16(uint32_t q, uint32_t (&o)[4]) {
+  const uint32_t lo = q ^ 0x88888888u, hi = lo >> 8;
+  constexpr uint32_t MAGIC = 0x64006400u;
+  uint32_t w0, w1, w2, w3;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(w0) : "r"(lo), "r"(0x000F000Fu), "r"(MAGIC));
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(w1) : "r"(lo), "r"(0x00F000F0u), "r"(MAGIC));
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(w2) : "r"(hi), "r"(0x000F000Fu), "r"(MAGIC));
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(w3) : "r"(hi), "r"(0x00F000F0u), "r"(MAGIC));
+  constexpr uint32_t SUB = 0x64086408u;    // 1032
+  constexpr uint32_t K16 = 0x2C002C00u;    // 1/16
+  constexpr uint32_t NEG72 = 0xD480D480u;  // -72
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(o[0]) : "r"(w0), "r"(SUB));
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(o[1]) : "r"(w1), "r"(K16), "r"(NEG72));
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(o[2]) : "r"(w2), "r"(SUB));
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(o[3]) : "r"(w3), "r"(K16), "r"(NEG72));
+}
+
+// True if any byte of v equals 0x00 or 0xFF (classic zero-byte test on v and ~v).
+__device__ __forceinline__ bool has_00_or_ff(uint32_t v) {
+  const uint32_t nv = ~v;
+  return (((v - 0x01010101u) & ~v) | ((nv - 0x01010101u) & ~nv)) & 0x80808080u;
+}
+
+// 2^(b-127) for an E8M0 byte b in 1..254 (callers route 0x00 / 0xFF through
+// the exact e8m0_decode).
+__device__ __forceinline__ float e8m0_fast(uint32_t word, int byte) {
+  return u2f(((word >> (8 * byte)) & 0xFFu) << 23);
+}
+
+// f16x2 broadcast of each of the two E4M3 bytes in the low half of v, exact
+// for normal E4M3 codes (exponent field 1..15, not the NaN code): f16 keeps
+// the sign, rebiases the exponent by +8 and widens the mantissa.  Returns
+// false when either byte is zero, subnormal or NaN (callers then use the
+// exact path).
+__device__ __forceinline__ bool e4m3x2_to_f16x2_fast(uint32_t v, uint32_t& lo, uint32_t& hi) {
+  const uint32_t e0 = (v >> 3) & 0xFu, e1 = (v >> 11) & 0xFu;
+  const uint32_t m0 = v & 0x7Fu, m1 = (v >> 8) & 0x7Fu;
+  const bool ok = e0 != 0 && e1 != 0 && m0 != 0x7Fu && m1 != 0x7Fu;
+  const uint32_t h0 = ((v & 0x80u) << 8) | ((m0 << 7) + 0x2000u);
+  const uint32_t h1 = ((v & 0x8000u)) | ((m1 << 7) + 0x2000u);
+  lo = h0 | (h0 << 16);
+  hi = h1 | (h1 << 16);
+  return ok;
+}
+
+__device__ __forceinline__ uint32_t f16x2_of(float f) {
+  const uint32_t h = (uint32_t)__half_as_ushort(__float2half_rn(f));  // exact for e4m3 values
+  return h | (h << 16);
+}
+
+// ---------------------------------------------------------------------------
+// X preparation
+// ---------------------------------------------------------------------------
+
+// One CTA per activation row.  For INT4 formats the f16 values of each group
+// of 8 are stored in the order (x0,x4,x1,x5,x2,x6,x3,x7) to match the
+// (c_i, c_i+4) pairs that int4x8_to_f16 produces.
+__global__ void __launch_bounds__(256) k_xprep(const uint16_t* __restrict__ X, int M, int K, int perm,
+                                               __half* __restrict__ Xh, float* __restrict__ xs) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  const int m = blockIdx.x;
+  __shared__ float red[8];
+  __shared__ float s_inv;
+  const uint16_t* xr = X + (size_t)m * K;
+  float amax = 0.0f;
+  for (int k = threadIdx.x * 8; k < K; k += blockDim.x * 8) {
+    const uint4 v = *reinterpret_cast<const uint4*>(xr + k);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    uint32_t w;
-    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(w) : "r"(u >> (4 * i)), "r"(0x000F000Fu), "r"(MAGIC));
-    o[i] = hsub2_bf16(w, BIAS);
+    for (int i = 0; i < 4; ++i) {
+      amax = fmaxf(amax, fabsf(u2f(w[i] << 16)));
+      amax = fmaxf(amax, fabsf(u2f(w[i] & 0xFFFF0000u)));
+    }
+  }
+#pragma unroll
+  for (int d = 16; d; d >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, d));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float a = 0.0f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) a = fmaxf(a, red[i]);
+    int s = 0;
+    if (a > 0.0f && isfinite(a)) {
+      s = ilogbf(a) - 14;
+      s = s < -126 ? -126 : (s > 114 ? 114 : s);
+    }
+    xs[m] = u2f((uint32_t)(127 + s) << 23);    // 2^s
+    s_inv = u2f((uint32_t)(127 - s) << 23);    // 2^-s
+  }
+  __syncthreads();
+  const float inv = s_inv;
+  for (int k = threadIdx.x * 8; k < K; k += blockDim.x * 8) {
+    const uint4 v = *reinterpret_cast<const uint4*>(xr + k);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    float f[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[2 * i] = u2f(w[i] << 16) * inv;
+      f[2 * i + 1] = u2f(w[i] & 0xFFFF0000u) * inv;
+    }
+    __half2 o[4];
+    if (perm) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) o[i] = __floats2half2_rn(f[i], f[i + 4]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) o[i] = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+    }
+    *reinterpret_cast<uint4*>(Xh + (size_t)m * K + k) = *reinterpret_cast<const uint4*>(o);
   }
 }
 
-// bf16x2 broadcast of an exact bf16 value given as fp32.
-__device__ __forceinline__ uint32_t bf16x2_of(float f) {
-  const uint32_t b = f2u(f) >> 16;  // exact for the values used here
-  return b | (b << 16);
-}
+// ---------------------------------------------------------------------------
+// The decode kernel
+// ---------------------------------------------------------------------------
 
-template <int FMT, int NT, int R, bool F32OUT>
-__global__ void __launch_bounds__(kWarpsPerCta * 32)
-k_gemv(const GemvArgs a) {
-  constexpr int TR = 16 * R;                  // rows per tile
-  constexpr int FRAG = R * NT * 4;            // accumulator floats per lane
+template <int FMT, int NT, bool F32OUT>
+__global__ void __launch_bounds__(kWarpsPerCta * 32) k_gemv(const GemvArgs a) {
+  constexpr int R = kRowTiles;
+  constexpr int FRAG = R * NT * 4;  // accumulator floats per lane
   const int lane = threadIdx.x & 31;
   const int w = blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5);
-  if (w >= a.W_total) return;
   const int g = lane >> 2, j = lane & 3;
   const int M = a.M, N = a.N, K = a.K, C = a.C;
-  const size_t rowb = (size_t)K / 2;          // packed bytes per row
-  const long long start = (long long)w * a.T / a.W_total;
-  const long long end = (long long)(w + 1) * a.T / a.W_total;
+  const size_t rowb = (size_t)K / 2;
+  const bool active = w < a.W_total;
+  const long long start = active ? (long long)w * a.T / a.W_total : 0;
+  const long long end = active ? (long long)(w + 1) * a.T / a.W_total : 0;
 
   float acc[R][NT][4];
 #pragma unroll
@@ -167,82 +273,95 @@ k_gemv(const GemvArgs a) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[r][t][e] = 0.0f;
 
-  // ---- per-iteration operands (double-buffered through registers) --------
-  uint4 wq[R][2];
-  uint32_t sc[R][2];  // raw scale bits per row (format dependent)
+  // Registers of one iteration: packed words and scale bits of rows g and
+  // g+8 of each row tile, and the X fragment of each n-tile.
+  uint32_t wq[R][2][4], sc[R][2];
   uint32_t xf[NT][16];
 
-  auto load = [&](long long it, uint4 (&wq_)[R][2], uint32_t (&sc_)[R][2], uint32_t (&xf_)[NT][16]) {
-    const int tile = (int)(it / C), c = (int)(it % C);
+  auto load_w = [&](int tile, int c) {
 #pragma unroll
     for (int r = 0; r < R; ++r)
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const int n = tile * TR + 16 * r + 8 * h + g;
-        wq_[r][h] = make_uint4(0, 0, 0, 0);
-        sc_[r][h] = 0;
+        const int n = tile * kTileRows + 16 * r + 8 * h + g;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) wq[r][h][q] = 0u;
+        sc[r][h] = 0u;
         if (n < N) {
           const uint8_t* row = a.data + (size_t)n * rowb + (size_t)c * (kChunkK / 2);
-          if (FMT == 3) {
+          if constexpr (FMT == 0) {  // 4 bytes of each of the 4 blocks
+#pragma unroll
+            for (int b = 0; b < 4; ++b) wq[r][h][b] = ldg_first4(row + 16 * b + 4 * j);
+            sc[r][h] = __ldg(reinterpret_cast<const uint32_t*>(static_cast<const uint8_t*>(a.scales) +
+                                                                (size_t)n * (K / 32) + 4 * c));
+          } else if constexpr (FMT == 3) {  // 8 bytes of each 64-group
             const uint2 lo = ldg_stream8(row + 8 * j), hi = ldg_stream8(row + 32 + 8 * j);
-            wq_[r][h] = make_uint4(lo.x, lo.y, hi.x, hi.y);
-          } else {
-            wq_[r][h] = ldg_stream(row + 16 * j);
-          }
-          if (FMT == 0) {
-            sc_[r][h] = __ldg(static_cast<const uint8_t*>(a.scales) + (size_t)n * (K / 32) + c * 4 + j);
-          } else if (FMT == 1) {
-            sc_[r][h] = __ldg(reinterpret_cast<const uint16_t*>(static_cast<const uint8_t*>(a.scales) +
-                                                                 (size_t)n * (K / 16) + c * 8 + 2 * j));
-          } else if (FMT == 2) {
-            sc_[r][h] = __ldg(static_cast<const uint16_t*>(a.scales) + (size_t)n * (K / 128) + c);
-          } else {
-            sc_[r][h] = __ldg(reinterpret_cast<const uint32_t*>(static_cast<const uint16_t*>(a.scales) +
-                                                                 (size_t)n * (K / 64) + 2 * c));
+            wq[r][h][0] = lo.x; wq[r][h][1] = lo.y; wq[r][h][2] = hi.x; wq[r][h][3] = hi.y;
+            sc[r][h] = __ldg(reinterpret_cast<const uint32_t*>(static_cast<const uint16_t*>(a.scales) +
+                                                                (size_t)n * (K / 64) + 2 * c));
+          } else {  // 16 contiguous bytes
+            const uint4 v = ldg_stream16(row + 16 * j);
+            wq[r][h][0] = v.x; wq[r][h][1] = v.y; wq[r][h][2] = v.z; wq[r][h][3] = v.w;
+            if constexpr (FMT == 1)
+              sc[r][h] = __ldg(reinterpret_cast<const uint16_t*>(static_cast<const uint8_t*>(a.scales) +
+                                                                  (size_t)n * (K / 16) + 8 * c + 2 * j));
+            else
+              sc[r][h] = __ldg(static_cast<const uint16_t*>(a.scales) + (size_t)n * (K / 128) + c);
           }
         }
       }
+  };
+  auto load_x = [&](int c) {
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
       const int m = 8 * t + g;
       if (m < M) {
-        const uint16_t* xr = a.X + (size_t)m * K + (size_t)c * kChunkK;
+        const __half* xr = a.Xh + (size_t)m * K + (size_t)c * kChunkK;
         uint4 v[4];
-        if (FMT == 3) {
-          v[0] = ldg_keep(xr + 16 * j); v[1] = ldg_keep(xr + 16 * j + 8);
-          v[2] = ldg_keep(xr + 64 + 16 * j); v[3] = ldg_keep(xr + 64 + 16 * j + 8);
+        if constexpr (FMT == 0) {
+#pragma unroll
+          for (int b = 0; b < 4; ++b) v[b] = ldg_keep16(xr + 32 * b + 8 * j);
+        } else if constexpr (FMT == 3) {
+          v[0] = ldg_keep16(xr + 16 * j); v[1] = ldg_keep16(xr + 16 * j + 8);
+          v[2] = ldg_keep16(xr + 64 + 16 * j); v[3] = ldg_keep16(xr + 64 + 16 * j + 8);
         } else {
 #pragma unroll
-          for (int q = 0; q < 4; ++q) v[q] = ldg_keep(xr + 32 * j + 8 * q);
+          for (int q = 0; q < 4; ++q) v[q] = ldg_keep16(xr + 32 * j + 8 * q);
         }
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          xf_[t][4 * q + 0] = v[q].x; xf_[t][4 * q + 1] = v[q].y;
-          xf_[t][4 * q + 2] = v[q].z; xf_[t][4 * q + 3] = v[q].w;
+          xf[t][4 * q] = v[q].x; xf[t][4 * q + 1] = v[q].y; xf[t][4 * q + 2] = v[q].z; xf[t][4 * q + 3] = v[q].w;
         }
       } else {
 #pragma unroll
-        for (int q = 0; q < 16; ++q) xf_[t][q] = 0u;
+        for (int q = 0; q < 16; ++q) xf[t][q] = 0u;
       }
     }
   };
 
   auto store_tile = [&](int tile, float (&v)[R][NT][4]) {
 #pragma unroll
-    for (int r = 0; r < R; ++r)
+    for (int t = 0; t < NT; ++t) {
+      float xsc[2];
 #pragma unroll
-      for (int t = 0; t < NT; ++t)
+      for (int e = 0; e < 2; ++e) {
+        const int m = 8 * t + 2 * j + e;
+        xsc[e] = (m < M) ? a.xs[m] : 0.0f;
+        if (FMT == 1) xsc[e] *= a.ts;
+      }
+#pragma unroll
+      for (int r = 0; r < R; ++r)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const int n = tile * TR + 16 * r + g + ((e & 2) ? 8 : 0);
+          const int n = tile * kTileRows + 16 * r + g + ((e & 2) ? 8 : 0);
           const int m = 8 * t + 2 * j + (e & 1);
           if (n < N && m < M) {
-            float y = v[r][t][e];
-            if (FMT == 1) y *= a.ts;
-            if (F32OUT) static_cast<float*>(a.Y)[(size_t)m * N + n] = y;
-            else static_cast<__nv_bfloat16*>(a.Y)[(size_t)m * N + n] = __float2bfloat16_rn(y);
+            const float y = v[r][t][e] * xsc[e & 1];
+            if (F32OUT) static_cast<float*>(a.Y)[(size_t)m * a.ldy + n] = y;
+            else static_cast<__nv_bfloat16*>(a.Y)[(size_t)m * a.ldy + n] = __float2bfloat16_rn(y);
           }
         }
+    }
   };
 
   auto slot_of = [&](int wid, int tile) -> size_t {
@@ -263,10 +382,10 @@ k_gemv(const GemvArgs a) {
                  make_float4(acc[r][t][0], acc[r][t][1], acc[r][t][2], acc[r][t][3]));
       __threadfence();
       __syncwarp();
-      unsigned ticket = 0;
       const long long t0 = (long long)tile * C, t1 = t0 + C - 1;
       const int w_lo = (int)(((t0 + 1) * a.W_total - 1) / a.T);
       const int w_hi = (int)(((t1 + 1) * a.W_total - 1) / a.T);
+      unsigned ticket = 0;
       if (lane == 0) ticket = atomicAdd(a.counters + tile, 1u);
       ticket = __shfl_sync(0xFFFFFFFFu, ticket, 0);
       if ((int)ticket == w_hi - w_lo) {  // last contributor: reduce in warp order
@@ -300,142 +419,150 @@ k_gemv(const GemvArgs a) {
         for (int e = 0; e < 4; ++e) acc[r][t][e] = 0.0f;
   };
 
+  // Weights do not depend on X: start streaming them before waiting for the
+  // X-preparation grid.
+  // (tile, c) of the current iteration and of the next one, advanced
+  // incrementally: no 64-bit division inside the loop.
+  int tile = (int)(start / C), c = (int)(start % C);
+  if (start < end) load_w(tile, c);
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   if (start >= end) return;
-  load(start, wq, sc, xf);
-  long long seg_begin = start;
+  load_x(c);
+
+  bool seg_full_start = (c == 0);
   for (long long it = start; it < end; ++it) {
-    const int tile = (int)(it / C), c = (int)(it % C);
-    uint4 cw[R][2];
-    uint32_t cs[R][2];
-    uint32_t cx[NT][16];
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      cw[r][0] = wq[r][0]; cw[r][1] = wq[r][1]; cs[r][0] = sc[r][0]; cs[r][1] = sc[r][1];
-    }
-#pragma unroll
-    for (int t = 0; t < NT; ++t)
-#pragma unroll
-      for (int q = 0; q < 16; ++q) cx[t][q] = xf[t][q];
-    if (it + 1 < end) load(it + 1, wq, sc, xf);
-
-    if (FMT >= 2) {  // INT4 operands are in (c_i, c_i+4) pair order
-#pragma unroll
-      for (int t = 0; t < NT; ++t)
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint32_t x0 = cx[t][4 * q], x1 = cx[t][4 * q + 1], x2 = cx[t][4 * q + 2], x3 = cx[t][4 * q + 3];
-          cx[t][4 * q + 0] = prmt(x0, x2, 0x5410u);
-          cx[t][4 * q + 1] = prmt(x0, x2, 0x7632u);
-          cx[t][4 * q + 2] = prmt(x1, x3, 0x5410u);
-          cx[t][4 * q + 3] = prmt(x1, x3, 0x7632u);
-        }
-    }
-
-    // per-row bf16x2 scale multipliers (MXFP4: one block, NVFP4: two blocks)
-    uint32_t smul[R][2][2];
-    bool slow[R][2];
+    int ntile = tile, nc = c + 1;
+    if (nc == C) { nc = 0; ++ntile; }
+    uint32_t cw[R][2][4], cs[R][2], cx[NT][16];
 #pragma unroll
     for (int r = 0; r < R; ++r)
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        slow[r][h] = false;
-        if (FMT == 0) {
-          const uint32_t sb = cs[r][h] & 0xFFu;
-          slow[r][h] = sb <= 1u;
-          const uint32_t b = (sb == 0xFFu) ? 0x7FC0u : (sb << 7);
-          smul[r][h][0] = smul[r][h][1] = b | (b << 16);
-        } else if (FMT == 1) {
-          smul[r][h][0] = bf16x2_of(e4m3_decode(cs[r][h] & 0xFFu));
-          smul[r][h][1] = bf16x2_of(e4m3_decode((cs[r][h] >> 8) & 0xFFu));
-        }
+        cs[r][h] = sc[r][h];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) cw[r][h][q] = wq[r][h][q];
       }
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+      for (int q = 0; q < 16; ++q) cx[t][q] = xf[t][q];
+    if (it + 1 < end) { load_w(ntile, nc); load_x(nc); }
 
-    float tmp[R][NT][4];
-    if (FMT >= 2) {
+    if constexpr (FMT == 0) {
+      // block b of the chunk = MMAs (b,0), (b,1); post-scale by 2^(e8m0-127)
+      bool special[R];
 #pragma unroll
-      for (int r = 0; r < R; ++r)
+      for (int r = 0; r < R; ++r) special[r] = has_00_or_ff(cs[r][0]) || has_00_or_ff(cs[r][1]);
 #pragma unroll
-        for (int t = 0; t < NT; ++t)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) tmp[r][t][e] = 0.0f;
-    }
-
-#pragma unroll
-    for (int qw = 0; qw < 4; ++qw) {  // 8 codes of each row per step = 2 MMAs
-      uint32_t A[R][2][4];
-#pragma unroll
-      for (int r = 0; r < R; ++r)
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const uint32_t q = (qw == 0) ? cw[r][h].x : (qw == 1) ? cw[r][h].y : (qw == 2) ? cw[r][h].z : cw[r][h].w;
-          if (FMT >= 2) {
-            int4x8_to_bf16(q, A[r][h]);
-          } else {
-            e2m1x8_to_bf16(q, A[r][h]);
-            const uint32_t m2 = smul[r][h][FMT == 1 ? (qw >> 1) : 0];
-            if (FMT == 0 && slow[r][h]) {
-              const float s = e8m0_decode(cs[r][h]);
-#pragma unroll
-              for (int p = 0; p < 4; ++p) {
-                const float f0 = e2m1_decode(q >> (8 * p)) * s, f1 = e2m1_decode(q >> (8 * p + 4)) * s;
-                A[r][h][p] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(f0)) |
-                             ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(f1)) << 16);
-              }
-            } else {
-#pragma unroll
-              for (int p = 0; p < 4; ++p) A[r][h][p] = hmul2_bf16(A[r][h][p], m2);
-            }
-          }
-        }
-#pragma unroll
-      for (int s = 0; s < 2; ++s) {
-        const int i = 2 * qw + s;  // MMA index within the chunk
+      for (int b = 0; b < 4; ++b) {
+        uint32_t A[R][2][4];
 #pragma unroll
         for (int r = 0; r < R; ++r)
 #pragma unroll
-          for (int t = 0; t < NT; ++t) {
-            float (&d)[4] = (FMT >= 2) ? tmp[r][t] : acc[r][t];
-            mma_bf16(d, A[r][0][2 * s], A[r][1][2 * s], A[r][0][2 * s + 1], A[r][1][2 * s + 1],
-                     cx[t][2 * i], cx[t][2 * i + 1]);
-          }
-      }
-      if (FMT == 3 && qw == 1) {  // end of the first 64-k group
+          for (int h = 0; h < 2; ++h) e2m1x8_to_f16(cw[r][h][b], A[r][h]);
 #pragma unroll
         for (int r = 0; r < R; ++r) {
-          const float s0 = fp16_bits_to_float(cs[r][0] & 0xFFFFu), s1 = fp16_bits_to_float(cs[r][1] & 0xFFFFu);
+          float s0 = e8m0_fast(cs[r][0], b), s1 = e8m0_fast(cs[r][1], b);
+          if (special[r]) {  // a 0x00 (2^-127) or 0xFF (NaN) scale in this chunk
+            s0 = e8m0_decode(cs[r][0] >> (8 * b));
+            s1 = e8m0_decode(cs[r][1] >> (8 * b));
+          }
 #pragma unroll
           for (int t = 0; t < NT; ++t) {
-            acc[r][t][0] = fmaf(s0, tmp[r][t][0], acc[r][t][0]);
-            acc[r][t][1] = fmaf(s0, tmp[r][t][1], acc[r][t][1]);
-            acc[r][t][2] = fmaf(s1, tmp[r][t][2], acc[r][t][2]);
-            acc[r][t][3] = fmaf(s1, tmp[r][t][3], acc[r][t][3]);
-            tmp[r][t][0] = tmp[r][t][1] = tmp[r][t][2] = tmp[r][t][3] = 0.0f;
+            float tmp[4];
+            mma_f16_z(tmp, A[r][0][0], A[r][1][0], A[r][0][1], A[r][1][1], cx[t][4 * b + 0], cx[t][4 * b + 1]);
+            mma_f16(tmp, A[r][0][2], A[r][1][2], A[r][0][3], A[r][1][3], cx[t][4 * b + 2], cx[t][4 * b + 3]);
+            acc[r][t][0] = fmaf(s0, tmp[0], acc[r][t][0]);
+            acc[r][t][1] = fmaf(s0, tmp[1], acc[r][t][1]);
+            acc[r][t][2] = fmaf(s1, tmp[2], acc[r][t][2]);
+            acc[r][t][3] = fmaf(s1, tmp[3], acc[r][t][3]);
           }
         }
       }
-    }
-    if (FMT >= 2) {
+    } else if constexpr (FMT == 1) {
+      // words 0,1 -> block 2j, words 2,3 -> block 2j+1; fold e4m3 into f16
+      uint32_t sw[R][2][2];
 #pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const uint32_t b0 = (FMT == 3) ? (cs[r][0] >> 16) : cs[r][0];
-        const uint32_t b1 = (FMT == 3) ? (cs[r][1] >> 16) : cs[r][1];
-        const float s0 = fp16_bits_to_float(b0 & 0xFFFFu), s1 = fp16_bits_to_float(b1 & 0xFFFFu);
+      for (int r = 0; r < R; ++r)
 #pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          acc[r][t][0] = fmaf(s0, tmp[r][t][0], acc[r][t][0]);
-          acc[r][t][1] = fmaf(s0, tmp[r][t][1], acc[r][t][1]);
-          acc[r][t][2] = fmaf(s1, tmp[r][t][2], acc[r][t][2]);
-          acc[r][t][3] = fmaf(s1, tmp[r][t][3], acc[r][t][3]);
+        for (int h = 0; h < 2; ++h)
+          if (!e4m3x2_to_f16x2_fast(cs[r][h], sw[r][h][0], sw[r][h][1])) {
+            sw[r][h][0] = f16x2_of(e4m3_decode(cs[r][h] & 0xFFu));
+            sw[r][h][1] = f16x2_of(e4m3_decode((cs[r][h] >> 8) & 0xFFu));
+          }
+#pragma unroll
+      for (int qw = 0; qw < 4; ++qw) {
+        uint32_t A[R][2][4];
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            e2m1x8_to_f16(cw[r][h][qw], A[r][h]);
+            const uint32_t m2 = sw[r][h][qw >> 1];
+#pragma unroll
+            for (int p = 0; p < 4; ++p) A[r][h][p] = hmul2_f16(A[r][h][p], m2);
+          }
+#pragma unroll
+        for (int s = 0; s < 2; ++s) {
+          const int i = 2 * qw + s;
+#pragma unroll
+          for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int t = 0; t < NT; ++t)
+              mma_f16(acc[r][t], A[r][0][2 * s], A[r][1][2 * s], A[r][0][2 * s + 1], A[r][1][2 * s + 1],
+                      cx[t][2 * i], cx[t][2 * i + 1]);
+        }
+      }
+    } else {
+      // INT4: FP32 partial per group, post-scaled by the FP16 group scale
+      float tmp[R][NT][4];
+#pragma unroll
+      for (int qw = 0; qw < 4; ++qw) {
+        uint32_t A[R][2][4];
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) int4x8_to_f16(cw[r][h][qw], A[r][h]);
+#pragma unroll
+        for (int s = 0; s < 2; ++s) {
+          const int i = 2 * qw + s;
+          const bool first = (FMT == 2) ? (i == 0) : (i == 0 || i == 4);
+#pragma unroll
+          for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+              if (first)
+                mma_f16_z(tmp[r][t], A[r][0][2 * s], A[r][1][2 * s], A[r][0][2 * s + 1], A[r][1][2 * s + 1],
+                          cx[t][2 * i], cx[t][2 * i + 1]);
+              else
+                mma_f16(tmp[r][t], A[r][0][2 * s], A[r][1][2 * s], A[r][0][2 * s + 1], A[r][1][2 * s + 1],
+                        cx[t][2 * i], cx[t][2 * i + 1]);
+            }
+        }
+        if ((FMT == 3 && qw == 1) || qw == 3) {  // end of a group
+          const int sh = (FMT == 3 && qw == 3) ? 16 : 0;
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            const float s0 = __half2float(__ushort_as_half((unsigned short)((cs[r][0] >> sh) & 0xFFFFu)));
+            const float s1 = __half2float(__ushort_as_half((unsigned short)((cs[r][1] >> sh) & 0xFFFFu)));
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+              acc[r][t][0] = fmaf(s0, tmp[r][t][0], acc[r][t][0]);
+              acc[r][t][1] = fmaf(s0, tmp[r][t][1], acc[r][t][1]);
+              acc[r][t][2] = fmaf(s1, tmp[r][t][2], acc[r][t][2]);
+              acc[r][t][3] = fmaf(s1, tmp[r][t][3], acc[r][t][3]);
+            }
+          }
         }
       }
     }
 
-    const bool tile_ends = (c == C - 1) || (it + 1 == end);
-    if (tile_ends) {
-      const bool full = ((seg_begin % C) == 0) && (c == C - 1);
-      flush(tile, full);
-      seg_begin = it + 1;
+    if (c == C - 1 || it + 1 == end) {
+      flush(tile, seg_full_start && (c == C - 1));
+      seg_full_start = true;  // the next segment starts at chunk 0
     }
+    tile = ntile;
+    c = nc;
   }
 }
 
@@ -444,25 +571,14 @@ k_gemv(const GemvArgs a) {
 // ---------------------------------------------------------------------------
 
 struct GemvPlan {
-  int fmt = 0, nt = 1, r = 2;
+  int fmt = 0, nt = 1;
   int tiles = 0, C = 0;
   long long T = 0;
   int grid = 0, W_total = 0;
-  size_t slot_floats = 0;
-  size_t partial_bytes = 0, counter_bytes = 0;
+  int mpad = 8;
+  size_t counter_bytes = 0, partial_bytes = 0, xs_bytes = 0, xh_bytes = 0;
+  size_t total() const { return counter_bytes + partial_bytes + xs_bytes + xh_bytes; }
 };
-
-template <int FMT, int NT, int R, bool F32>
-static int occupancy_of() {
-  static int occ = 0;
-  if (occ == 0) {
-    int v = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, k_gemv<FMT, NT, R, F32>, kWarpsPerCta * 32, 0) != cudaSuccess || v < 1)
-      v = 1;
-    occ = v;
-  }
-  return occ;
-}
 
 static int fmt_code(int32_t format) {
   switch (format) {
@@ -474,23 +590,28 @@ static int fmt_code(int32_t format) {
   return -1;
 }
 
-static void pick_tile(int M, int* nt, int* r) {
-  if (M <= 8) { *nt = 1; *r = 2; }
-  else if (M <= 16) { *nt = 2; *r = 2; }
-  else { *nt = 4; *r = 1; }
+template <int FMT, int NT>
+static int occupancy_of() {
+  static int occ[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 1;
+  if (occ[dev] == 0) {
+    int v = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, k_gemv<FMT, NT, false>, kWarpsPerCta * 32, 0) !=
+            cudaSuccess || v < 1)
+      v = 1;
+    occ[dev] = v;
+  }
+  return occ[dev];
 }
 
-// Occupancy is a property of the compiled kernel; approximate with the
-// bf16-out instance of each (FMT, NT, R) (both outputs use the same registers
-// to within a few).
 template <int FMT>
-static int occ_for(int nt, int r) {
-  if (nt == 1) return occupancy_of<FMT, 1, 2, false>();
-  if (nt == 2) return occupancy_of<FMT, 2, 2, false>();
-  return occupancy_of<FMT, 4, 1, false>();
-}
+static int occ_for(int nt) { return nt == 1 ? occupancy_of<FMT, 1>() : occupancy_of<FMT, 2>(); }
 
-qgemm_status_t gemv_plan(const qgemm_weights_t* w, int M, GemvPlan* p) {
+static size_t pad256(size_t b) { return (b + 255) & ~(size_t)255; }
+
+// Plan for one launch over mb (<= 16) activation rows.
+qgemm_status_t gemv_plan(const qgemm_weights_t* w, int mb, GemvPlan* p) {
   const int f = fmt_code(w->format);
   if (f < 0) return fail(QGEMM_ERR_INVALID_ARG, "gemm: unknown format %d", (int)w->format);
   if (w->K == 0 || w->N == 0) return fail(QGEMM_ERR_INVALID_ARG, "gemm: empty weight matrix");
@@ -501,104 +622,109 @@ qgemm_status_t gemv_plan(const qgemm_weights_t* w, int M, GemvPlan* p) {
   DevProps dp;
   qgemm_status_t st = device_props(&dp);
   if (st != QGEMM_OK) return st;
-  const int mb = M > 32 ? 32 : M;
-  pick_tile(mb, &p->nt, &p->r);
   p->fmt = f;
-  p->tiles = (int)((w->N + 16 * p->r - 1) / (16 * p->r));
+  p->nt = mb <= 8 ? 1 : 2;
+  p->mpad = 8 * p->nt;
+  p->tiles = (int)((w->N + kTileRows - 1) / kTileRows);
   p->C = (int)(w->K / kChunkK);
   p->T = (long long)p->tiles * p->C;
   int occ = 1;
   switch (f) {
-    case 0: occ = occ_for<0>(p->nt, p->r); break;
-    case 1: occ = occ_for<1>(p->nt, p->r); break;
-    case 2: occ = occ_for<2>(p->nt, p->r); break;
-    default: occ = occ_for<3>(p->nt, p->r); break;
+    case 0: occ = occ_for<0>(p->nt); break;
+    case 1: occ = occ_for<1>(p->nt); break;
+    case 2: occ = occ_for<2>(p->nt); break;
+    default: occ = occ_for<3>(p->nt); break;
   }
   long long warps = (long long)dp.sm_count * occ * kWarpsPerCta;
   if (warps > p->T) warps = p->T;
   p->W_total = (int)warps;
   p->grid = (int)((warps + kWarpsPerCta - 1) / kWarpsPerCta);
-  p->slot_floats = (size_t)p->r * p->nt * 4 * 32;
-  p->partial_bytes = 2 * (size_t)p->W_total * p->slot_floats * sizeof(float);
-  p->counter_bytes = ((size_t)p->tiles * sizeof(unsigned) + 255) & ~(size_t)255;
+  const size_t slot = (size_t)kRowTiles * p->nt * 4 * 32 * sizeof(float);
+  p->counter_bytes = pad256((size_t)p->tiles * sizeof(unsigned));
+  p->partial_bytes = pad256(2 * (size_t)p->W_total * slot);
+  p->xs_bytes = pad256((size_t)kMaxM * sizeof(float));
+  p->xh_bytes = pad256((size_t)kMaxM * w->K * sizeof(__half));
   return QGEMM_OK;
 }
 
 template <int FMT, bool F32>
-static void launch_fmt(const GemvPlan& p, const GemvArgs& a, cudaStream_t s) {
-  if (p.nt == 1) k_gemv<FMT, 1, 2, F32><<<p.grid, kWarpsPerCta * 32, 0, s>>>(a);
-  else if (p.nt == 2) k_gemv<FMT, 2, 2, F32><<<p.grid, kWarpsPerCta * 32, 0, s>>>(a);
-  else k_gemv<FMT, 4, 1, F32><<<p.grid, kWarpsPerCta * 32, 0, s>>>(a);
+static cudaError_t launch_fmt(const GemvPlan& p, const GemvArgs& a, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)p.grid);
+  cfg.blockDim = dim3(kWarpsPerCta * 32);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (p.nt == 1) return cudaLaunchKernelEx(&cfg, k_gemv<FMT, 1, F32>, a);
+  return cudaLaunchKernelEx(&cfg, k_gemv<FMT, 2, F32>, a);
 }
 
 template <bool F32>
-static void launch_gemv(const GemvPlan& p, const GemvArgs& a, cudaStream_t s) {
+static cudaError_t launch_gemv(const GemvPlan& p, const GemvArgs& a, cudaStream_t s) {
   switch (p.fmt) {
-    case 0: launch_fmt<0, F32>(p, a, s); break;
-    case 1: launch_fmt<1, F32>(p, a, s); break;
-    case 2: launch_fmt<2, F32>(p, a, s); break;
-    default: launch_fmt<3, F32>(p, a, s); break;
+    case 0: return launch_fmt<0, F32>(p, a, s);
+    case 1: return launch_fmt<1, F32>(p, a, s);
+    case 2: return launch_fmt<2, F32>(p, a, s);
+    default: return launch_fmt<3, F32>(p, a, s);
   }
 }
 
 static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Workspace layout: [counters (256-byte padded)][partials].
-qgemm_status_t gemm_decode(const qgemm_weights_t* w, const uint16_t* X, int M, void* Y, bool f32,
-                           void* ws, size_t ws_bytes, cudaStream_t s) {
+qgemm_status_t gemm_decode(const qgemm_weights_t* w, const uint16_t* X, int M, void* Y, bool f32, void* ws,
+                           size_t ws_bytes, cudaStream_t s) {
   if (!w || !X || !Y) return fail(QGEMM_ERR_INVALID_ARG, "gemm: null pointer");
   if (M < 1) return fail(QGEMM_ERR_INVALID_ARG, "gemm: M must be >= 1");
   if (!w->data || !w->scales) return fail(QGEMM_ERR_INVALID_ARG, "gemm: null weight pointer");
   if (w->reserved != 0) return fail(QGEMM_ERR_INVALID_ARG, "gemm: reserved field must be 0");
-  if (w->format == QGEMM_FMT_NVFP4 && !(std::isfinite(w->tensor_scale)))
+  if (w->format == QGEMM_FMT_NVFP4 && !std::isfinite(w->tensor_scale))
     return fail(QGEMM_ERR_INVALID_ARG, "gemm: NVFP4 tensor_scale must be finite");
   GemvPlan p;
-  qgemm_status_t st = gemv_plan(w, M, &p);
+  qgemm_status_t st = gemv_plan(w, M < kMaxM ? M : kMaxM, &p);
   if (st != QGEMM_OK) return st;
-  if (!al16(w->data) || !al16(X) || (w->format == QGEMM_FMT_NVFP4 && (reinterpret_cast<uintptr_t>(w->scales) & 1u)) ||
-      ((w->format == QGEMM_FMT_INT4_G128 || w->format == QGEMM_FMT_INT4_G64) &&
-       (reinterpret_cast<uintptr_t>(w->scales) & 3u)))
-    return fail(QGEMM_ERR_INVALID_ARG, "gemm: data and X must be 16-byte aligned, scales naturally aligned");
-  const size_t need = p.counter_bytes + p.partial_bytes;
-  if (!ws || ws_bytes < need)
-    return fail(QGEMM_ERR_WORKSPACE, "gemm: workspace of %zu bytes needed, %zu given", need, ws_bytes);
+  const uintptr_t sa = reinterpret_cast<uintptr_t>(w->scales);
+  const bool scales_ok = (w->format == QGEMM_FMT_NVFP4) ? (sa & 1u) == 0 : (sa & 3u) == 0;
+  if (!al16(w->data) || !al16(X) || !scales_ok)
+    return fail(QGEMM_ERR_INVALID_ARG, "gemm: data and X must be 16-byte aligned, scales 4-byte aligned");
+  if (!ws || !al16(ws) || ws_bytes < p.total())
+    return fail(QGEMM_ERR_WORKSPACE, "gemm: 16-byte aligned workspace of %zu bytes needed, %zu given", p.total(),
+                ws_bytes);
+  uint8_t* base = static_cast<uint8_t*>(ws);
   GemvArgs a;
-  a.data = w->data; a.scales = w->scales; a.N = (int)w->N; a.K = (int)w->K;
+  a.data = w->data; a.scales = w->scales; a.N = (int)w->N; a.K = (int)w->K; a.ldy = (int)w->N;
   a.ts = w->tensor_scale;
-  a.counters = static_cast<unsigned*>(ws);
-  a.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + p.counter_bytes);
-  a.T = p.T; a.C = p.C; a.W_total = p.W_total;
-  for (int m0 = 0; m0 < M; m0 += 32) {
-    const int mb = (M - m0) < 32 ? (M - m0) : 32;
-    GemvPlan pb = p;
-    pick_tile(mb, &pb.nt, &pb.r);
-    if (pb.nt != p.nt) {  // last partial block may use a narrower tile
-      st = gemv_plan(w, mb, &pb);
-      if (st != QGEMM_OK) return st;
-      if (pb.counter_bytes + pb.partial_bytes > ws_bytes)
-        return fail(QGEMM_ERR_WORKSPACE, "gemm: workspace too small for the tail block");
-      a.T = pb.T; a.C = pb.C; a.W_total = pb.W_total;
-      a.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + pb.counter_bytes);
-    }
-    a.M = mb;
-    a.X = X + (size_t)m0 * w->K;
+  a.counters = reinterpret_cast<unsigned*>(base);
+  a.partials = reinterpret_cast<float*>(base + p.counter_bytes);
+  float* xs = reinterpret_cast<float*>(base + p.counter_bytes + p.partial_bytes);
+  __half* xh = reinterpret_cast<__half*>(base + p.counter_bytes + p.partial_bytes + p.xs_bytes);
+  a.xs = xs; a.Xh = xh;
+  const int perm = (w->format == QGEMM_FMT_INT4_G128 || w->format == QGEMM_FMT_INT4_G64) ? 1 : 0;
+  for (int m0 = 0; m0 < M; m0 += kMaxM) {
+    const int mb = (M - m0) < kMaxM ? (M - m0) : kMaxM;
+    GemvPlan pb;
+    st = gemv_plan(w, mb, &pb);
+    if (st != QGEMM_OK) return st;
+    a.T = pb.T; a.C = pb.C; a.W_total = pb.W_total; a.M = mb;
     a.Y = f32 ? (void*)(static_cast<float*>(Y) + (size_t)m0 * w->N)
               : (void*)(static_cast<uint16_t*>(Y) + (size_t)m0 * w->N);
-    if (f32) launch_gemv<true>(pb, a, s);
-    else launch_gemv<false>(pb, a, s);
+    k_xprep<<<mb, 256, 0, s>>>(X + (size_t)m0 * w->K, mb, (int)w->K, perm, xh, xs);
     QG_LAUNCH_RET();
+    const cudaError_t e = f32 ? launch_gemv<true>(pb, a, s) : launch_gemv<false>(pb, a, s);
+    if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "gemm: launch failed: %s", cudaGetErrorString(e));
   }
   return QGEMM_OK;
 }
 
 size_t gemm_decode_workspace(const qgemm_weights_t* w, int M) {
   GemvPlan p;
-  if (!w || gemv_plan(w, M, &p) != QGEMM_OK) return 0;
-  size_t need = p.counter_bytes + p.partial_bytes;
-  if (M > 32 && (M % 32) != 0) {
+  if (!w || M < 1 || gemv_plan(w, M < kMaxM ? M : kMaxM, &p) != QGEMM_OK) return 0;
+  size_t need = p.total();
+  if (M > kMaxM && (M % kMaxM) != 0) {  // the tail block may plan differently
     GemvPlan q;
-    if (gemv_plan(w, M % 32, &q) == QGEMM_OK && q.counter_bytes + q.partial_bytes > need)
-      need = q.counter_bytes + q.partial_bytes;
+    if (gemv_plan(w, M % kMaxM, &q) == QGEMM_OK && q.total() > need) need = q.total();
   }
   return need;
 }
@@ -617,13 +743,13 @@ qgemm_status_t qgemm_workspace_init(void* ws, size_t ws_bytes, void* stream) {
   return QGEMM_OK;
 }
 
-qgemm_status_t qgemm_gemm_w4a16(const qgemm_weights_t* w, const uint16_t* X, int32_t M, uint16_t* Y,
-                                void* ws, size_t ws_bytes, void* stream) {
+qgemm_status_t qgemm_gemm_w4a16(const qgemm_weights_t* w, const uint16_t* X, int32_t M, uint16_t* Y, void* ws,
+                                size_t ws_bytes, void* stream) {
   return gemm_decode(w, X, M, Y, false, ws, ws_bytes, as_stream(stream));
 }
 
-qgemm_status_t qgemm_gemm_w4a16_f32(const qgemm_weights_t* w, const uint16_t* X, int32_t M, float* Y,
-                                    void* ws, size_t ws_bytes, void* stream) {
+qgemm_status_t qgemm_gemm_w4a16_f32(const qgemm_weights_t* w, const uint16_t* X, int32_t M, float* Y, void* ws,
+                                    size_t ws_bytes, void* stream) {
   return gemm_decode(w, X, M, Y, true, ws, ws_bytes, as_stream(stream));
 }
 
