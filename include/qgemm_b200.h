@@ -131,6 +131,10 @@ qgemm_status_t qgemm_gemm_w4a16_f32(const qgemm_weights_t* w, const uint16_t* X,
                                     int32_t M, float* Y, void* workspace,
                                     size_t ws_bytes, void* stream);
 
+/* Synchronous: reports (and returns QGEMM_ERR_TIMEOUT) if a bounded barrier
+ * wait inside the tcgen05 GEMM kernel gave up on this device.  Not capturable. */
+qgemm_status_t qgemm_umma_status(int32_t* faulted);
+
 /* ---- baselines and probes (bench harness; not on the product path) ------- */
 /* cuBLAS BF16 dense Y[M,N] = X[M,K] . W[N,K]^T (bench_cublas.cu:144-151 with
  * CUDA_R_16BF in place of CUDA_R_16F, COMPUTE_32F). */

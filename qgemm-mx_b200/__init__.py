@@ -75,6 +75,7 @@ _sig("qgemm_cublas_bf16_gemm", _i32, [_vp, _vp, _i32, _sz, _sz, _vp, _vp])
 _sig("qgemm_probe_launch", _i32, [_i32, _vp, _vp, _sz, _vp])
 _sig("qgemm_device_info", _i32, [C.POINTER(_i32), C.POINTER(_sz)])
 _sig("qgemm_probe_status", _i32, [C.POINTER(_i32)])
+_sig("qgemm_umma_status", _i32, [C.POINTER(_i32)])
 
 EXPORTED = [n for n in dir(_lib) if n.startswith("qgemm_")]
 
@@ -322,6 +323,12 @@ def probe_status() -> None:
     """Raises QGemmError if a bounded wait inside a TMA bulk probe gave up."""
     f = _i32(0)
     _check(_lib.qgemm_probe_status(C.byref(f)), "probe_status")
+
+
+def umma_status() -> None:
+    """Raises QGemmError if a bounded wait inside the tcgen05 kernel gave up."""
+    f = _i32(0)
+    _check(_lib.qgemm_umma_status(C.byref(f)), "umma_status")
 
 
 def device_info() -> tuple[int, int]:

@@ -674,6 +674,14 @@ static cudaError_t launch_gemv(const GemvPlan& p, const GemvArgs& a, cudaStream_
 
 static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+qgemm_status_t gemm_umma(const qgemm_weights_t* w, const uint16_t* X, int M, void* Y, bool f32, cudaStream_t s);
+
+// The tcgen05 path takes MXFP4 / NVFP4 with M >= 64 and K % 64 == 0 (below
+// that the decode kernel streams W faster); it needs no workspace.
+static bool use_umma(const qgemm_weights_t* w, int M) {
+  return M >= 64 && (w->format == QGEMM_FMT_MXFP4 || w->format == QGEMM_FMT_NVFP4) && w->K % 64 == 0;
+}
+
 qgemm_status_t gemm_decode(const qgemm_weights_t* w, const uint16_t* X, int M, void* Y, bool f32, void* ws,
                            size_t ws_bytes, cudaStream_t s) {
   if (!w || !X || !Y) return fail(QGEMM_ERR_INVALID_ARG, "gemm: null pointer");
@@ -689,6 +697,11 @@ qgemm_status_t gemm_decode(const qgemm_weights_t* w, const uint16_t* X, int M, v
   const bool scales_ok = (w->format == QGEMM_FMT_NVFP4) ? (sa & 1u) == 0 : (sa & 3u) == 0;
   if (!al16(w->data) || !al16(X) || !scales_ok)
     return fail(QGEMM_ERR_INVALID_ARG, "gemm: data and X must be 16-byte aligned, scales 4-byte aligned");
+  if (use_umma(w, M)) {
+    if (w->format == QGEMM_FMT_NVFP4 && (sa & 3u) != 0)
+      return fail(QGEMM_ERR_INVALID_ARG, "gemm: NVFP4 scales must be 4-byte aligned");
+    return gemm_umma(w, X, M, Y, f32, s);
+  }
   if (!ws || !al16(ws) || ws_bytes < p.total())
     return fail(QGEMM_ERR_WORKSPACE, "gemm: 16-byte aligned workspace of %zu bytes needed, %zu given", p.total(),
                 ws_bytes);
@@ -719,6 +732,7 @@ qgemm_status_t gemm_decode(const qgemm_weights_t* w, const uint16_t* X, int M, v
 }
 
 size_t gemm_decode_workspace(const qgemm_weights_t* w, int M) {
+  if (w && use_umma(w, M)) return 256;
   GemvPlan p;
   if (!w || M < 1 || gemv_plan(w, M < kMaxM ? M : kMaxM, &p) != QGEMM_OK) return 0;
   size_t need = p.total();
