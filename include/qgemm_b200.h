@@ -131,6 +131,19 @@ qgemm_status_t qgemm_gemm_w4a16_f32(const qgemm_weights_t* w, const uint16_t* X,
                                     int32_t M, float* Y, void* workspace,
                                     size_t ws_bytes, void* stream);
 
+/* Y = X . W^T (bf16 out) without a workspace argument, for callers that
+ * cannot provide one: an operator slot that passes only inputs, outputs and a
+ * stream, a plugin inside a framework that owns the device memory pool and
+ * forbids raw cudaMalloc, or code running while another component captures
+ * the stream in global mode.  No counterpart in the reference (its host path
+ * never needs device scratch).  Scratch is a fixed 16 MiB device array per
+ * GPU held until exit; larger plans return QGEMM_ERR_WORKSPACE.  The first
+ * call on a device looks up that array (make it before any stream capture);
+ * every call shares it, so calls that may overlap on the GPU race.  Always
+ * runs the decode kernel; allocates nothing. */
+qgemm_status_t qgemm_gemm_w4a16_noalloc(const qgemm_weights_t* w, const uint16_t* X,
+                                        int32_t M, uint16_t* Y, void* stream);
+
 /* Synchronous: reports (and returns QGEMM_ERR_TIMEOUT) if a bounded barrier
  * wait inside the tcgen05 GEMM kernel gave up on this device.  Not capturable. */
 qgemm_status_t qgemm_umma_status(int32_t* faulted);

@@ -71,6 +71,7 @@ _sig("qgemm_workspace_size", _sz, [C.POINTER(_Weights), _i32])
 _sig("qgemm_workspace_init", _i32, [_vp, _sz, _vp])
 _sig("qgemm_gemm_w4a16", _i32, [C.POINTER(_Weights), _vp, _i32, _vp, _vp, _sz, _vp])
 _sig("qgemm_gemm_w4a16_f32", _i32, [C.POINTER(_Weights), _vp, _i32, _vp, _vp, _sz, _vp])
+_sig("qgemm_gemm_w4a16_noalloc", _i32, [C.POINTER(_Weights), _vp, _i32, _vp, _vp])
 _sig("qgemm_cublas_bf16_gemm", _i32, [_vp, _vp, _i32, _sz, _sz, _vp, _vp])
 _sig("qgemm_probe_launch", _i32, [_i32, _vp, _vp, _sz, _vp])
 _sig("qgemm_device_info", _i32, [C.POINTER(_i32), C.POINTER(_sz)])

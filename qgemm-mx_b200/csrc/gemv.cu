@@ -768,3 +768,98 @@ qgemm_status_t qgemm_gemm_w4a16_f32(const qgemm_weights_t* w, const uint16_t* X,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free decode GEMM
+// ---------------------------------------------------------------------------
+//
+// Some callers cannot hand the library a workspace: an operator slot whose
+// fixed signature carries only inputs, outputs and a stream; a plugin running
+// inside a host framework that owns the device memory pool and forbids raw
+// cudaMalloc; code that runs while another component captures the stream in
+// global mode, where cudaMalloc is an unsafe call.  For them the decode
+// kernel's scratch (split-tile partial sums, tile tickets, the f16 copy of X)
+// lives in a fixed device array that the library reserves once.
+//
+// Properties:
+//  * 16 MiB of device memory per GPU that loads the library, held until the
+//    process exits.  Calls whose plan needs more scratch (about K > 300k, or a
+//    device with far more SMs) return QGEMM_ERR_WORKSPACE.
+//  * The first call on each device looks up the array's device address with
+//    cudaGetSymbolAddress; make that first call before any stream capture.
+//  * Every call shares the array: calls that may overlap on the GPU (other
+//    streams, other threads) race and must be serialised by the caller.
+//  * The tile tickets that must start at zero are cleared by each call
+//    (cudaMemsetAsync on the caller's stream); nothing is allocated.
+//  * Always runs the decode kernel (any M, in blocks of 16 activation rows).
+
+namespace qg {
+
+constexpr size_t kNoAllocScratchBytes = (size_t)16 << 20;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+static qgemm_status_t noalloc_scratch(uint8_t** out) {
+  static uint8_t* ptrs[64] = {nullptr};
+  int dev = 0;
+  QG_CUDA_RET(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(QGEMM_ERR_CUDA, "gemm_noalloc: device ordinal %d out of range", dev);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(QGEMM_ERR_CUDA, "gemm_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+    ptrs[dev] = static_cast<uint8_t*>(p);
+  }
+  *out = ptrs[dev];
+  return QGEMM_OK;
+}
+
+}  // namespace qg
+
+extern "C" qgemm_status_t qgemm_gemm_w4a16_noalloc(const qgemm_weights_t* w, const uint16_t* X, int32_t M,
+                                                   uint16_t* Y, void* stream) {
+  using namespace qg;
+  cudaStream_t s = as_stream(stream);
+  if (!w || !X || !Y) return fail(QGEMM_ERR_INVALID_ARG, "gemm_noalloc: null pointer");
+  if (M < 1) return fail(QGEMM_ERR_INVALID_ARG, "gemm_noalloc: M must be >= 1");
+  if (!w->data || !w->scales) return fail(QGEMM_ERR_INVALID_ARG, "gemm_noalloc: null weight pointer");
+  if (w->reserved != 0) return fail(QGEMM_ERR_INVALID_ARG, "gemm_noalloc: reserved field must be 0");
+  if (w->format == QGEMM_FMT_NVFP4 && !std::isfinite(w->tensor_scale))
+    return fail(QGEMM_ERR_INVALID_ARG, "gemm_noalloc: NVFP4 tensor_scale must be finite");
+  GemvPlan p;
+  qgemm_status_t st = gemv_plan(w, M < kMaxM ? M : kMaxM, &p);
+  if (st != QGEMM_OK) return st;
+  const uintptr_t sa = reinterpret_cast<uintptr_t>(w->scales);
+  const bool scales_ok = (w->format == QGEMM_FMT_NVFP4) ? (sa & 1u) == 0 : (sa & 3u) == 0;
+  if (!al16(w->data) || !al16(X) || !scales_ok)
+    return fail(QGEMM_ERR_INVALID_ARG, "gemm_noalloc: data and X must be 16-byte aligned, scales 4-byte aligned");
+  if (p.total() > kNoAllocScratchBytes)
+    return fail(QGEMM_ERR_WORKSPACE, "gemm_noalloc: needs %zu bytes of scratch, the fixed array holds %zu",
+                p.total(), kNoAllocScratchBytes);
+  uint8_t* base = nullptr;
+  st = noalloc_scratch(&base);
+  if (st != QGEMM_OK) return st;
+  QG_CUDA_RET(cudaMemsetAsync(base, 0, p.counter_bytes, s));
+  GemvArgs a;
+  a.data = w->data; a.scales = w->scales; a.N = (int)w->N; a.K = (int)w->K; a.ldy = (int)w->N;
+  a.ts = w->tensor_scale;
+  a.counters = reinterpret_cast<unsigned*>(base);
+  a.partials = reinterpret_cast<float*>(base + p.counter_bytes);
+  float* xs = reinterpret_cast<float*>(base + p.counter_bytes + p.partial_bytes);
+  __half* xh = reinterpret_cast<__half*>(base + p.counter_bytes + p.partial_bytes + p.xs_bytes);
+  a.xs = xs; a.Xh = xh;
+  const int perm = (w->format == QGEMM_FMT_INT4_G128 || w->format == QGEMM_FMT_INT4_G64) ? 1 : 0;
+  for (int m0 = 0; m0 < M; m0 += kMaxM) {
+    const int mb = (M - m0) < kMaxM ? (M - m0) : kMaxM;
+    GemvPlan pb;
+    st = gemv_plan(w, mb, &pb);
+    if (st != QGEMM_OK) return st;
+    a.T = pb.T; a.C = pb.C; a.W_total = pb.W_total; a.M = mb;
+    a.Y = static_cast<uint16_t*>(Y) + (size_t)m0 * w->N;
+    k_xprep<<<mb, 256, 0, s>>>(X + (size_t)m0 * w->K, mb, (int)w->K, perm, xh, xs);
+    QG_LAUNCH_RET();
+    const cudaError_t e = launch_gemv<false>(pb, a, s);
+    if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "gemm_noalloc: launch failed: %s", cudaGetErrorString(e));
+  }
+  return QGEMM_OK;
+}
