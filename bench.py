@@ -61,6 +61,9 @@ def parse():
     ap.add_argument("--workload", default="llama70b_mxfp4", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--table", action="store_true", help="print the per-(layer, M) table to stderr")
+    ap.add_argument("--prefill", action="store_true",
+                    help="compute-bound table: NVFP4 (28672,8192) and (8192,28672), M in {2048,4096,8192}, "
+                         "tcgen05 path vs cuBLAS BF16 of the same shape")
     ap.add_argument("--case", default=None,
                     help="fmt,N,K,M: run only that GEMM --steps times (for profilers), print its mean time")
     return ap.parse_args()
@@ -94,6 +97,67 @@ def run_case(args):
     us = a.elapsed_time(b) * 1e3 / args.steps
     nb = qg.total_bytes(fcode, M, N, K)
     print(json.dumps({"case": args.case, "us_per_call": round(us, 3), "gbs": round(nb / us / 1e3, 1)}))
+
+
+def run_prefill(args):
+    """TFLOP/s of the tcgen05 path on the compute-bound shapes, next to a
+    cuBLAS BF16 GEMM of the same shape (weights dequantised to bf16), both
+    timed as CUDA-graph replays with CUDA events, against the measured BF16
+    peak.  Prints a table to stderr and one JSON line."""
+    import torch
+    qg = importlib.import_module("qgemm-mx_b200")
+    peak = 1632.0
+    pp = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(pp):
+        with open(pp) as f:
+            peak = float(json.load(f)["bf16_tflops"])
+    gen = torch.Generator(device="cuda")
+    rows = []
+    for (N, K) in [(28672, 8192), (8192, 28672)]:
+        gen.manual_seed(N + K)
+        W = torch.randn((N, K), generator=gen, device="cuda").mul_(0.02)
+        p = qg.pack(qg.NVFP4, W)
+        del W
+        Wb = qg.dequant(p).to(torch.bfloat16)
+        for M in [2048, 4096, 8192]:
+            X = torch.randn((M, K), generator=gen, device="cuda").to(torch.bfloat16)
+            Y = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+            Yc = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+            ws = qg.make_workspace(p, M)
+
+            def timed(fn, reps=5):
+                s = torch.cuda.Stream()
+                s.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(s):
+                    for _ in range(2):
+                        fn()
+                torch.cuda.current_stream().wait_stream(s)
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    for _ in range(reps):
+                        fn()
+                g.replay()
+                torch.cuda.synchronize()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                g.replay()
+                b.record()
+                torch.cuda.synchronize()
+                return a.elapsed_time(b) / reps * 1e-3
+
+            t_ours = timed(lambda: qg.gemm_w4a16(p, X, out=Y, workspace=ws))
+            t_cub = timed(lambda: qg.cublas_bf16_gemm(Wb, X, out=Yc))
+            fl = 2.0 * M * N * K
+            rows.append({"N": N, "K": K, "M": M, "ours_tflops": round(fl / t_ours / 1e12, 1),
+                         "cublas_bf16_tflops": round(fl / t_cub / 1e12, 1),
+                         "ours_frac_of_peak": round(fl / t_ours / 1e12 / peak, 4),
+                         "ours_over_cublas": round(t_cub / t_ours, 3)})
+            print(json.dumps(rows[-1]), file=sys.stderr, flush=True)
+            del X, Y, Yc, ws
+        del p, Wb
+        torch.cuda.empty_cache()
+    print(json.dumps({"prefill": rows, "bf16_peak_tflops": peak}))
 
 
 def fmt_code(qg, name):
@@ -255,6 +319,9 @@ def main():
     args = parse()
     if args.case:
         run_case(args)
+        return
+    if args.prefill:
+        run_prefill(args)
         return
     if args.impl == "reference":
         run_reference_arm(args)

@@ -674,12 +674,25 @@ static cudaError_t launch_gemv(const GemvPlan& p, const GemvArgs& a, cudaStream_
 
 static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-qgemm_status_t gemm_umma(const qgemm_weights_t* w, const uint16_t* X, int M, void* Y, bool f32, cudaStream_t s);
+qgemm_status_t gemm_umma_ts(const qgemm_weights_t* w, const __half* Xh, const float* xs, int M, void* Y, bool f32,
+                            int splits, void* split_ws, cudaStream_t s);
+int umma_splits(const qgemm_weights_t* w, int M, int sm_count);
+size_t umma_split_workspace(const qgemm_weights_t* w, int M, int splits);
 
-// The tcgen05 path takes MXFP4 / NVFP4 with M >= 64 and K % 64 == 0 (below
-// that the decode kernel streams W faster); it needs no workspace.
+// The tcgen05 path (dequantised W in TMEM) takes MXFP4 / NVFP4 with M >= 32
+// and K % 64 == 0.  Its workspace holds the f16 copy of X and the row factors.
 static bool use_umma(const qgemm_weights_t* w, int M) {
-  return M >= 64 && (w->format == QGEMM_FMT_MXFP4 || w->format == QGEMM_FMT_NVFP4) && w->K % 64 == 0;
+  return M >= 32 && (w->format == QGEMM_FMT_MXFP4 || w->format == QGEMM_FMT_NVFP4) && w->K % 64 == 0;
+}
+static int umma_split_count(const qgemm_weights_t* w, int M) {
+  DevProps dp;
+  if (device_props(&dp) != QGEMM_OK) return 1;
+  return umma_splits(w, M, dp.sm_count);
+}
+// [xs | Xh | split-K counters and partials]
+static size_t umma_workspace(const qgemm_weights_t* w, int M) {
+  return pad256((size_t)M * sizeof(float)) + pad256((size_t)M * w->K * sizeof(__half)) +
+         umma_split_workspace(w, M, umma_split_count(w, M));
 }
 
 qgemm_status_t gemm_decode(const qgemm_weights_t* w, const uint16_t* X, int M, void* Y, bool f32, void* ws,
@@ -698,9 +711,17 @@ qgemm_status_t gemm_decode(const qgemm_weights_t* w, const uint16_t* X, int M, v
   if (!al16(w->data) || !al16(X) || !scales_ok)
     return fail(QGEMM_ERR_INVALID_ARG, "gemm: data and X must be 16-byte aligned, scales 4-byte aligned");
   if (use_umma(w, M)) {
-    if (w->format == QGEMM_FMT_NVFP4 && (sa & 3u) != 0)
-      return fail(QGEMM_ERR_INVALID_ARG, "gemm: NVFP4 scales must be 4-byte aligned");
-    return gemm_umma(w, X, M, Y, f32, s);
+    const size_t need = umma_workspace(w, M);
+    if (!ws || !al16(ws) || ws_bytes < need)
+      return fail(QGEMM_ERR_WORKSPACE, "gemm: 16-byte aligned workspace of %zu bytes needed, %zu given", need,
+                  ws_bytes);
+    float* xs = static_cast<float*>(ws);
+    __half* xh = reinterpret_cast<__half*>(static_cast<uint8_t*>(ws) + pad256((size_t)M * sizeof(float)));
+    void* split_ws = static_cast<uint8_t*>(ws) + pad256((size_t)M * sizeof(float)) +
+                     pad256((size_t)M * w->K * sizeof(__half));
+    k_xprep<<<M, 256, 0, s>>>(X, M, (int)w->K, 0, xh, xs);
+    QG_LAUNCH_RET();
+    return gemm_umma_ts(w, xh, xs, M, Y, f32, umma_split_count(w, M), split_ws, s);
   }
   if (!ws || !al16(ws) || ws_bytes < p.total())
     return fail(QGEMM_ERR_WORKSPACE, "gemm: 16-byte aligned workspace of %zu bytes needed, %zu given", p.total(),
@@ -732,7 +753,7 @@ qgemm_status_t gemm_decode(const qgemm_weights_t* w, const uint16_t* X, int M, v
 }
 
 size_t gemm_decode_workspace(const qgemm_weights_t* w, int M) {
-  if (w && use_umma(w, M)) return 256;
+  if (w && use_umma(w, M)) return umma_workspace(w, M);
   GemvPlan p;
   if (!w || M < 1 || gemv_plan(w, M < kMaxM ? M : kMaxM, &p) != QGEMM_OK) return 0;
   size_t need = p.total();

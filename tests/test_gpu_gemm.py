@@ -72,6 +72,40 @@ def test_gemm_stream_k_shapes(qg, cuda, O, orc, N, K):
             assert ok, (fmt, M, ratio, rel)
 
 
+@pytest.mark.parametrize("fmt,group", [("mxfp4", 32), ("nvfp4", 16)])
+@pytest.mark.parametrize("M", [32, 64, 200])
+def test_gemm_split_k_tcgen05(qg, cuda, O, orc, fmt, group, M):
+    """Few 128-row tiles and a long K: the tcgen05 path splits K across CTAs
+    and reduces the FP32 partials in split order (deterministic)."""
+    N, K = 300, 8192
+    p, d, s, ts = packed_pair(qg, O, orc, fmt, group, N, K, seed=M)
+    X = O.randn_bf16(M, 2, M * K).reshape(M, K)
+    Yref = orc.w4a16_gemm(fmt, d, s, N, K, X, group=group, tensor_scale=ts, nthreads=8)
+    Xd = to_dev_bf16(X)
+    ws = qg.make_workspace(p, M)
+    a = qg.gemm_w4a16(p, Xd, workspace=ws, out_f32=True).cpu().numpy()
+    b = qg.gemm_w4a16(p, Xd, workspace=ws, out_f32=True).cpu().numpy()
+    assert same_bits(a, b)
+    ok, ratio, rel = within_tolerance(a, Yref)
+    assert ok and rel < 1e-5, (ratio, rel)
+
+
+def test_gemm_mxfp4_wide_scale_rows(qg, cuda, O, orc):
+    """MXFP4 rows whose blocks span ~30 binades (1e-9 next to 1): the tcgen05
+    path folds block scales relative to a per-row base exponent."""
+    N, K, M = 256, 1024, 64
+    W = weights(O, N, K, seed=11)
+    W[:, :256] *= 1e-9
+    W[::3, 512:544] *= 1000.0
+    Wd = to_dev_f32(W)
+    p = qg.pack_mxfp4(Wd)
+    d, s = u8(p.data), u8(p.scales)
+    X = O.randn_bf16(3, 2, M * K).reshape(M, K)
+    Yref = orc.w4a16_gemm("mxfp4", d, s, N, K, X, nthreads=8)
+    ok, ratio, rel = within_tolerance(run(qg, p, X, f32=True), Yref)
+    assert ok and rel < 1e-5, (ratio, rel)
+
+
 def test_gemm_deterministic_and_scaling(qg, cuda, O, orc):
     N, K, M = 3000, 4096, 8
     for fmt, group in FORMATS:
