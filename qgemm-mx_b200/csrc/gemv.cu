@@ -193,10 +193,25 @@ __device__ __forceinline__ uint32_t f16x2_of(float f) {
 // One CTA per activation row.  For INT4 formats the f16 values of each group
 // of 8 are stored in the order (x0,x4,x1,x5,x2,x6,x3,x7) to match the
 // (c_i, c_i+4) pairs that int4x8_to_f16 produces.
-__global__ void __launch_bounds__(256) k_xprep(const uint16_t* __restrict__ X, int M, int K, int perm,
+// swz_bn > 0 selects the tcgen05 operand layout instead: for each block of
+// swz_bn activation rows and each 64-k block, swz_bn rows of 128 bytes whose
+// 16-byte chunk c is stored at chunk c ^ (row % 8) -- the shared-memory image
+// of a 128-byte-swizzled K-major tile, so one linear bulk copy stages it.
+// Rows M .. ceil(M / swz_bn) * swz_bn - 1 (one CTA each) are written as zeros.
+__device__ __forceinline__ size_t xprep_index(int m, int k, int K, int swz_bn) {
+  if (swz_bn == 0) return (size_t)m * K + k;
+  const int mb = m / swz_bn, r = m % swz_bn, kb = k >> 6, c = (k >> 3) & 7;
+  return (((size_t)mb * (K >> 6) + kb) * swz_bn + r) * 64 + (size_t)((c ^ (r & 7)) << 3);
+}
+__global__ void __launch_bounds__(256) k_xprep(const uint16_t* __restrict__ X, int M, int K, int perm, int swz_bn,
                                                __half* __restrict__ Xh, float* __restrict__ xs) {
   asm volatile("griddepcontrol.launch_dependents;");
   const int m = blockIdx.x;
+  if (m >= M) {  // zero padding rows of the last activation block
+    for (int k = threadIdx.x * 8; k < K; k += blockDim.x * 8)
+      *reinterpret_cast<uint4*>(Xh + xprep_index(m, k, K, swz_bn)) = make_uint4(0u, 0u, 0u, 0u);
+    return;
+  }
   __shared__ float red[8];
   __shared__ float s_inv;
   const uint16_t* xr = X + (size_t)m * K;
@@ -244,7 +259,7 @@ __global__ void __launch_bounds__(256) k_xprep(const uint16_t* __restrict__ X, i
 #pragma unroll
       for (int i = 0; i < 4; ++i) o[i] = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
     }
-    *reinterpret_cast<uint4*>(Xh + (size_t)m * K + k) = *reinterpret_cast<const uint4*>(o);
+    *reinterpret_cast<uint4*>(Xh + xprep_index(m, k, K, swz_bn)) = *reinterpret_cast<const uint4*>(o);
   }
 }
 
@@ -679,20 +694,40 @@ qgemm_status_t gemm_umma_ts(const qgemm_weights_t* w, const __half* Xh, const fl
 int umma_splits(const qgemm_weights_t* w, int M, int sm_count);
 size_t umma_split_workspace(const qgemm_weights_t* w, int M, int splits);
 
-// The tcgen05 path (dequantised W in TMEM) takes MXFP4 / NVFP4 with M >= 32
-// and K % 64 == 0.  Its workspace holds the f16 copy of X and the row factors.
+bool umma_sk_supported(const qgemm_weights_t* w, int M);
+int umma_sk_bn(int M);
+size_t umma_sk_workspace(const qgemm_weights_t* w, int M, int sm_count);
+qgemm_status_t gemm_umma_sk(const qgemm_weights_t* w, const __half* Xh, const float* xs, int M, void* Y, bool f32,
+                            void* ws, int sm_count, cudaStream_t s);
+
+// The tcgen05 paths (dequantised W in TMEM) take MXFP4 / NVFP4 with M >= 32:
+// the persistent stream-K kernel for M < 256 and K % 128 == 0 (umma_sk.cu),
+// the tile-per-CTA kernel with K splits otherwise (K % 64 == 0, umma.cu).
+// Their workspace holds the f16 copy of X, its row factors and the split
+// tiles' tickets and partial sums.
 static bool use_umma(const qgemm_weights_t* w, int M) {
   return M >= 32 && (w->format == QGEMM_FMT_MXFP4 || w->format == QGEMM_FMT_NVFP4) && w->K % 64 == 0;
 }
-static int umma_split_count(const qgemm_weights_t* w, int M) {
+static int sm_count_or_zero() {
   DevProps dp;
-  if (device_props(&dp) != QGEMM_OK) return 1;
-  return umma_splits(w, M, dp.sm_count);
+  return device_props(&dp) == QGEMM_OK ? dp.sm_count : 0;
 }
-// [xs | Xh | split-K counters and partials]
+static int umma_split_count(const qgemm_weights_t* w, int M) {
+  const int sms = sm_count_or_zero();
+  return sms > 0 ? umma_splits(w, M, sms) : 1;
+}
+// [xs | Xh | split tickets and partials]
+static size_t umma_xh_bytes(const qgemm_weights_t* w, int M) {
+  const int rows = umma_sk_supported(w, M) ? (M + umma_sk_bn(M) - 1) / umma_sk_bn(M) * umma_sk_bn(M) : M;
+  return pad256((size_t)rows * w->K * sizeof(__half));
+}
 static size_t umma_workspace(const qgemm_weights_t* w, int M) {
-  return pad256((size_t)M * sizeof(float)) + pad256((size_t)M * w->K * sizeof(__half)) +
-         umma_split_workspace(w, M, umma_split_count(w, M));
+  const size_t head = pad256((size_t)M * sizeof(float)) + umma_xh_bytes(w, M);
+  if (umma_sk_supported(w, M)) {
+    const int sms = sm_count_or_zero();
+    return sms > 0 ? head + umma_sk_workspace(w, M, sms) : 0;
+  }
+  return head + umma_split_workspace(w, M, umma_split_count(w, M));
 }
 
 qgemm_status_t gemm_decode(const qgemm_weights_t* w, const uint16_t* X, int M, void* Y, bool f32, void* ws,
@@ -717,9 +752,14 @@ qgemm_status_t gemm_decode(const qgemm_weights_t* w, const uint16_t* X, int M, v
                   ws_bytes);
     float* xs = static_cast<float*>(ws);
     __half* xh = reinterpret_cast<__half*>(static_cast<uint8_t*>(ws) + pad256((size_t)M * sizeof(float)));
-    void* split_ws = static_cast<uint8_t*>(ws) + pad256((size_t)M * sizeof(float)) +
-                     pad256((size_t)M * w->K * sizeof(__half));
-    k_xprep<<<M, 256, 0, s>>>(X, M, (int)w->K, 0, xh, xs);
+    void* split_ws = static_cast<uint8_t*>(ws) + pad256((size_t)M * sizeof(float)) + umma_xh_bytes(w, M);
+    if (umma_sk_supported(w, M)) {
+      const int bn = umma_sk_bn(M);
+      k_xprep<<<(M + bn - 1) / bn * bn, 256, 0, s>>>(X, M, (int)w->K, 0, bn, xh, xs);
+      QG_LAUNCH_RET();
+      return gemm_umma_sk(w, xh, xs, M, Y, f32, split_ws, sm_count_or_zero(), s);
+    }
+    k_xprep<<<M, 256, 0, s>>>(X, M, (int)w->K, 0, 0, xh, xs);
     QG_LAUNCH_RET();
     return gemm_umma_ts(w, xh, xs, M, Y, f32, umma_split_count(w, M), split_ws, s);
   }
@@ -744,7 +784,7 @@ qgemm_status_t gemm_decode(const qgemm_weights_t* w, const uint16_t* X, int M, v
     a.T = pb.T; a.C = pb.C; a.W_total = pb.W_total; a.M = mb;
     a.Y = f32 ? (void*)(static_cast<float*>(Y) + (size_t)m0 * w->N)
               : (void*)(static_cast<uint16_t*>(Y) + (size_t)m0 * w->N);
-    k_xprep<<<mb, 256, 0, s>>>(X + (size_t)m0 * w->K, mb, (int)w->K, perm, xh, xs);
+    k_xprep<<<mb, 256, 0, s>>>(X + (size_t)m0 * w->K, mb, (int)w->K, perm, 0, xh, xs);
     QG_LAUNCH_RET();
     const cudaError_t e = f32 ? launch_gemv<true>(pb, a, s) : launch_gemv<false>(pb, a, s);
     if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "gemm: launch failed: %s", cudaGetErrorString(e));
@@ -877,7 +917,7 @@ extern "C" qgemm_status_t qgemm_gemm_w4a16_noalloc(const qgemm_weights_t* w, con
     if (st != QGEMM_OK) return st;
     a.T = pb.T; a.C = pb.C; a.W_total = pb.W_total; a.M = mb;
     a.Y = static_cast<uint16_t*>(Y) + (size_t)m0 * w->N;
-    k_xprep<<<mb, 256, 0, s>>>(X + (size_t)m0 * w->K, mb, (int)w->K, perm, xh, xs);
+    k_xprep<<<mb, 256, 0, s>>>(X + (size_t)m0 * w->K, mb, (int)w->K, perm, 0, xh, xs);
     QG_LAUNCH_RET();
     const cudaError_t e = launch_gemv<false>(pb, a, s);
     if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "gemm_noalloc: launch failed: %s", cudaGetErrorString(e));

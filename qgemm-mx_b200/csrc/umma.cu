@@ -28,6 +28,7 @@
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
+#include "tc.cuh"
 
 namespace qg {
 
@@ -36,7 +37,6 @@ __device__ unsigned g_umma_fault = 0;
 constexpr int kUBM = 128;  // weight rows per tile (UMMA M)
 constexpr int kUBK = 64;   // K per stage (one 128-byte swizzle row of bf16)
 constexpr int kUThreads = 192;
-constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s
 
 struct UmmaArgs {
   const void* scales;
@@ -52,76 +52,15 @@ struct UmmaArgs {
 // PTX wrappers
 // ---------------------------------------------------------------------------
 
-__device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-__device__ __forceinline__ unsigned long long gtimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-               : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
-  return ok != 0;
-}
 // Bounded wait; false (and the fault flag set) when the phase never completes.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-  if (mbar_try(bar, parity)) return true;
-  const unsigned long long t0 = gtimer();
-  while (!mbar_try(bar, parity)) {
-    if (gtimer() - t0 > kWaitNs) {
-      atomicExch(&g_umma_fault, 1u);
-      return false;
-    }
-  }
-  return true;
+  return mbar_wait_flag(bar, parity, &g_umma_fault);
 }
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
-      : "memory");
-}
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-
-// K-major, SWIZZLE_128B shared-memory matrix descriptor: 8-row atoms of
-// 128-byte rows, 1024 bytes apart (stride byte offset), version 1.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
-  return (uint64_t)((addr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
-// Instruction descriptor: kind::f16, A = B = bf16, D = f32, both K-major.
-__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
-}
-
 __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
   asm volatile(
       "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }"
       ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
-}
-__device__ __forceinline__ void umma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t s) {
@@ -372,53 +311,6 @@ constexpr int kTsAStages = 4;            // TMEM A stages of 32 columns each
 // TMEM columns: accumulator (BN) + A stages; 256 lets two CTAs share an SM.
 __host__ __device__ constexpr uint32_t ts_tmem_cols(int bn) { return bn + 32 * kTsAStages <= 256 ? 256u : 512u; }
 
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[16]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
-      ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
-        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
-      : "memory");
-}
-__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p; }"
-      ::"r"(tmem_d), "r"(tmem_a), "l"(b), "r"(idesc), "r"(acc)
-      : "memory");
-}
-// kind::f16 instruction descriptor with f16 A and B (format code 0).
-__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
-  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
-}
-__device__ __forceinline__ void e2m1x8_to_f16_ts(uint32_t q, uint32_t* o) {
-  asm("{ .reg .b8 b0, b1, b2, b3;\n"
-      "  mov.b32 {b0, b1, b2, b3}, %4;\n"
-      "  cvt.rn.f16x2.e2m1x2 %0, b0;\n"
-      "  cvt.rn.f16x2.e2m1x2 %1, b1;\n"
-      "  cvt.rn.f16x2.e2m1x2 %2, b2;\n"
-      "  cvt.rn.f16x2.e2m1x2 %3, b3; }\n"
-      : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3])
-      : "r"(q));
-}
-__device__ __forceinline__ uint32_t hmul2_f16_ts(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-// f16x2 broadcast of 2^e: normal for e >= -14, subnormal down to 2^-24,
-// zero below.  (e <= 13 by construction.)
-__device__ __forceinline__ uint32_t f16x2_pow2(int e) {
-  uint32_t h;
-  if (e >= -14) h = (uint32_t)(e + 15) << 10;
-  else if (e >= -24) h = 1u << (e + 24);
-  else h = 0u;
-  return h | (h << 16);
-}
-// f16x2 broadcast of an E4M3 value (exact; NaN code -> f16 NaN).
-__device__ __forceinline__ uint32_t f16x2_e4m3(uint32_t b) {
-  const uint32_t h = (uint32_t)__half_as_ushort(__float2half_rn(e4m3_decode(b & 0xFFu)));
-  return h | (h << 16);
-}
-
 template <int FMT, int BN, int STAGES, bool F32OUT>
 __global__ void __launch_bounds__(kTsThreads, 2)
 k_umma_ts(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x, const UmmaArgs a,
@@ -565,16 +457,16 @@ k_umma_ts(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUt
       const uint4 pk = *reinterpret_cast<const uint4*>(P_ptr(s) + r * 32 + 16 * h);  // 32 codes
       const uint32_t qw[4] = {pk.x, pk.y, pk.z, pk.w};
 #pragma unroll
-      for (int w4 = 0; w4 < 4; ++w4) e2m1x8_to_f16_ts(qw[w4], o + 4 * w4);
+      for (int w4 = 0; w4 < 4; ++w4) e2m1x8_to_f16x2(qw[w4], o + 4 * w4);
       if (FMT == 0) {
         const uint32_t b = sc & 0xFFu;
         const uint32_t f = (b == 0xFFu) ? 0x7E007E00u : f16x2_pow2((int)b - 127 - rbase);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) o[i] = hmul2_f16_ts(o[i], f);
+        for (int i = 0; i < 16; ++i) o[i] = hmul2_f16x2(o[i], f);
       } else {
         const uint32_t f0 = f16x2_e4m3(sc & 0xFFu), f1 = f16x2_e4m3((sc >> 8) & 0xFFu);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) o[i] = hmul2_f16_ts(o[i], i < 8 ? f0 : f1);
+        for (int i = 0; i < 16; ++i) o[i] = hmul2_f16x2(o[i], i < 8 ? f0 : f1);
       }
       return true;
     };
@@ -584,7 +476,7 @@ k_umma_ts(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUt
     if (ksteps > 0) ok = produce(0, load_scale(kbeg), cur);
     for (int ks = 0; ks < ksteps && ok; ++ks) {
       const int sa = ks % kTsAStages;
-      tmem_st32(tmem_a + ((uint32_t)(32 * q) << 16) + (uint32_t)(sa * 32 + 16 * h), cur);
+      tmem_st16(tmem_a + ((uint32_t)(32 * q) << 16) + (uint32_t)(sa * 32 + 16 * h), cur);
       if (ks + 1 < ksteps) ok = produce(ks + 1, load_scale(kbeg + ks + 1), nxt);
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
@@ -674,7 +566,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-static bool make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr, uint64_t inner, uint64_t outer,
+bool make_tma_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr, uint64_t inner, uint64_t outer,
                         uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
   auto fn = encode_fn();
   if (!fn) return false;
@@ -763,9 +655,9 @@ qgemm_status_t gemm_umma(const qgemm_weights_t* w, const uint16_t* X, int M, voi
     return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "umma path: K must be a multiple of %d", kUBK);
   const int bn = umma_bn_for(M);
   CUtensorMap mw, mx;
-  if (!make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->data, w->K / 2, w->N, w->K / 2, kUBK / 2, kUBM,
+  if (!make_tma_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->data, w->K / 2, w->N, w->K / 2, kUBK / 2, kUBM,
                    CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, X, w->K, (uint64_t)M, w->K * 2, kUBK, (uint32_t)bn,
+      !make_tma_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, X, w->K, (uint64_t)M, w->K * 2, kUBK, (uint32_t)bn,
                    CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(QGEMM_ERR_CUDA, "umma path: cuTensorMapEncodeTiled failed");
   UmmaArgs a;
@@ -805,9 +697,9 @@ qgemm_status_t gemm_umma_ts(const qgemm_weights_t* w, const __half* Xh, const fl
     return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "umma path: K must be a multiple of %d", kUBK);
   const int bn = umma_bn_for(M);
   CUtensorMap mw, mx;
-  if (!make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->data, w->K / 2, w->N, w->K / 2, kUBK / 2, kUBM,
+  if (!make_tma_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->data, w->K / 2, w->N, w->K / 2, kUBK / 2, kUBM,
                    CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, Xh, w->K, (uint64_t)M, w->K * 2, kUBK, (uint32_t)bn,
+      !make_tma_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, Xh, w->K, (uint64_t)M, w->K * 2, kUBK, (uint32_t)bn,
                    CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(QGEMM_ERR_CUDA, "umma path: cuTensorMapEncodeTiled failed");
   UmmaArgs a;
@@ -829,6 +721,8 @@ qgemm_status_t gemm_umma_ts(const qgemm_weights_t* w, const __half* Xh, const fl
   return QGEMM_OK;
 }
 
+unsigned umma_sk_fault();
+
 }  // namespace qg
 
 using namespace qg;
@@ -838,6 +732,9 @@ extern "C" {
 qgemm_status_t qgemm_umma_status(int32_t* faulted) {
   unsigned f = 0;
   QG_CUDA_RET(cudaMemcpyFromSymbol(&f, g_umma_fault, sizeof(f)));
+  const unsigned g = umma_sk_fault();
+  if (g == 0xFFFFFFFFu) return fail(QGEMM_ERR_CUDA, "umma: reading the stream-K fault flag failed");
+  f |= g;
   if (faulted) *faulted = (int32_t)f;
   return f ? fail(QGEMM_ERR_TIMEOUT, "umma: a bounded barrier wait gave up") : QGEMM_OK;
 }

@@ -1,0 +1,605 @@
+// umma_sk.cu -- persistent stream-K tcgen05 W4A16 GEMM for 32 <= M < 128
+// (MXFP4 / NVFP4, K % 256 == 0).
+//
+// Y[M,N] = X[M,K] . W[N,K]^T with W in the reference's packed layouts
+// (titoatwork/qgemm-mx include/qgemm/pack.hpp:14-85); X arrives as the f16
+// copy with per-row power-of-two factors xs[m] made by k_xprep (gemv.cu).
+//
+// Swap-AB: 128 weight rows are the UMMA M side, BN (32 / 64) activation rows
+// the N side; the FP32 accumulator D = Y^T tile lives in TMEM.  The
+// dequantised operand never touches shared memory: each dequant thread widens
+// its row's codes with cvt.rn.f16x2.e2m1x2, folds the block scale with one
+// f16x2 multiply and writes TMEM with tcgen05.st; the MMA takes A from TMEM
+// and B (X) from shared memory (kind::f16, TS form).
+//   NVFP4  e2m1 * e4m3 is exact in f16; the FP32 tensor scale is applied in
+//          the epilogue.
+//   MXFP4  2^(e8m0-127) is folded relative to a per-row, per-segment base
+//          b = max(e8m0) - 140 over the segment's blocks, so every factor is
+//          <= 2^13 and e2m1 * factor <= 49152 fits f16; products are exact
+//          while e8m0 >= max - 36 and blocks further down are flushed to
+//          zero.  The epilogue multiplies row n by 2^b.
+//
+// Schedule: one CTA per SM, stream-K.  The iteration space (tile, 256-k step)
+// is cut into one contiguous range per CTA; a CTA walks its range as
+// segments (a tile's run of steps).  A segment covering a whole tile is
+// stored directly; a partial segment parks its FP32 tile (already scaled by
+// its row factors) in the workspace, and the CTA whose ticket shows it
+// arrived last sums all contributors in CTA order (deterministic).
+//
+// Pacing.  A tcgen05.mma with N <= 64 occupies the tensor pipe ~45 cycles
+// whatever N, and the issuing thread blocks for that long; 128 weight rows x
+// 256 k (16 MMAs, ~720 cycles) is also what HBM delivers to one SM in that
+// time.  So each barrier round trip is amortised over 16 MMAs, and the packed
+// W ring is released by the dequant warps as soon as they have read a stage
+// (not by the MMAs), so its depth covers HBM latency on its own.
+//
+// Warp roles (768 threads):
+//   warp 0        X producer: one linear bulk copy per step of the X tile
+//                 (four BN x 64 f16 sub-tiles, already in the 128-byte
+//                 swizzled image k_xprep wrote) into the X ring.
+//   warps 1, 2    W producers, alternate steps: one packed-W box per step by
+//                 TMA (128 rows x 128 B, 128-byte swizzle) into the W ring.
+//                 (A TMA-issuing thread streams about one box row per 8
+//                 cycles; two keep ahead of HBM.)  No multicast anywhere.
+//   warp 3        TMEM allocation (512 columns) and the MMA issuer: 16
+//                 tcgen05.mma (K = 16) per step into accumulator buffer
+//                 seg & 1; commits release the X stage, the TMEM A stage and,
+//                 at a segment's end, the accumulator.
+//   warps 4..19   dequant: warp w covers TMEM lane quadrant w % 4 (32 weight
+//                 rows) and 64-k slice (w - 4) / 4 of each step.
+//   warps 20..23  epilogue: drain accumulator buffers (double-buffered, so
+//                 the next segment's MMAs overlap the drain), split-tile
+//                 tickets and reductions; ahead of each segment they compute
+//                 the MXFP4 row bases (or prefetch NVFP4 scales into L2).
+// TMEM: [acc 0 | acc 1 | AST A stages of 128 columns (256 k, f16 pairs)].
+//
+// Every mbarrier wait is bounded (tc.cuh); on timeout the kernel sets
+// g_sk_fault, lets copies in flight land, frees TMEM and returns.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "tc.cuh"
+
+namespace qg {
+
+__device__ unsigned g_sk_fault = 0;
+
+constexpr int kSkBK = 256;                               // k per pipeline step
+constexpr int kSkRows = 128;                             // weight rows per tile
+constexpr int kSkXProd = 0;
+constexpr int kSkWProd0 = 1, kSkWProds = 2;
+constexpr int kSkMmaWarp = 3;
+constexpr int kSkDqWarp0 = 4;
+constexpr int kSkDqWarps = 16;
+constexpr int kSkEpiWarps = 4;
+constexpr int kSkEpiWarp0 = kSkDqWarp0 + kSkDqWarps;
+constexpr int kSkThreads = 32 * (kSkEpiWarp0 + kSkEpiWarps);  // 768
+constexpr int kSkScaleAhead = 8;                         // scale prefetch distance (steps)
+
+template <int BN>
+struct SkCfg {
+  static constexpr int W_STAGE = kSkRows * kSkBK / 2;    // 16 KB packed codes
+  static constexpr int XBOX = BN * 128;                  // 64 k of X (f16), one swizzle row per activation row
+  static constexpr int X_STAGE = 4 * XBOX;
+  static constexpr int SX = BN == 32 ? 4 : 3;            // X ring depth
+  static constexpr int SW = BN == 32 ? 8 : 6;            // W ring depth (even: two W producers)
+  static constexpr int AST = (512 - 2 * BN) / 128;       // TMEM A stages
+  static constexpr int NBAR = 2 * SX + 2 * SW + 2 * AST + 8;
+  static constexpr int BYTES = 1024 + SX * X_STAGE + SW * W_STAGE + NBAR * 8 + 2 * kSkRows * 4 + 16;
+  static_assert(BYTES <= 232448, "shared memory");
+  static_assert(2 * BN + 128 * AST <= 512, "TMEM columns");
+  static_assert(SW % kSkWProds == 0, "each W producer owns whole stages");
+};
+
+struct SkArgs {
+  const uint8_t* scales;
+  const uint8_t* xsw;   // X in the swizzled operand layout (k_xprep with swz_bn = BN)
+  void* Y;
+  const float* xs;
+  float* partials;      // [2 * G][128][BN] FP32, scaled by the row factors
+  unsigned* counters;   // [tiles] tickets (start and end at zero)
+  long long T;          // tiles * KS
+  int M, N, K;
+  int tiles_n;          // tile t -> rows (t % tiles_n) * 128, activations (t / tiles_n) * BN
+  int KS;               // steps per tile (K / 128)
+  int G;                // CTAs
+  float ts;
+};
+
+// Largest E8M0 byte among nbytes scale bytes at p, with NaN codes (0xFF)
+// counted as 0.  p is 4-byte aligned and nbytes a multiple of 4.
+__device__ __forceinline__ int e8m0_row_max(const uint8_t* p, int nbytes) {
+  uint32_t m4 = 0;
+  auto fold = [&](uint32_t v) { m4 = __vmaxu4(m4, v & ~__vcmpeq4(v, 0xFFFFFFFFu)); };
+  int i = 0;
+  while (i < nbytes && (reinterpret_cast<uintptr_t>(p + i) & 15u)) {
+    fold(__ldg(reinterpret_cast<const uint32_t*>(p + i)));
+    i += 4;
+  }
+  for (; i + 128 <= nbytes; i += 128) {
+    uint4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = __ldg(reinterpret_cast<const uint4*>(p + i) + u);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) { fold(v[u].x); fold(v[u].y); fold(v[u].z); fold(v[u].w); }
+  }
+  for (; i + 16 <= nbytes; i += 16) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(p + i));
+    fold(v.x); fold(v.y); fold(v.z); fold(v.w);
+  }
+  for (; i < nbytes; i += 4) fold(__ldg(reinterpret_cast<const uint32_t*>(p + i)));
+  m4 = __vmaxu4(m4, m4 >> 16);
+  m4 = __vmaxu4(m4, m4 >> 8);
+  return (int)(m4 & 0xFFu);
+}
+
+template <int FMT, int BN, bool F32OUT>
+__global__ void __launch_bounds__(kSkThreads, 1)
+k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
+  using C = SkCfg<BN>;
+  constexpr int SX = C::SX, SW = C::SW, AST = C::AST;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = su32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;  // swizzled tiles want 1024-byte alignment
+  uint8_t* gbase = smem_raw + (base - raw);
+  // [X ring: SX x (four BN x 128 B sub-tiles)] [W ring: SW x (128 rows x 128 B)]
+  auto X_addr = [&](int s) { return base + (uint32_t)(s * C::X_STAGE); };
+  auto W_off = [&](int s) { return SX * C::X_STAGE + s * C::W_STAGE; };
+  uint64_t* bars = reinterpret_cast<uint64_t*>(gbase + SX * C::X_STAGE + SW * C::W_STAGE);
+  auto fullx_bar = [&](int s) { return su32(&bars[s]); };
+  auto emptyx_bar = [&](int s) { return su32(&bars[SX + s]); };
+  auto fullw_bar = [&](int s) { return su32(&bars[2 * SX + s]); };
+  auto emptyw_bar = [&](int s) { return su32(&bars[2 * SX + SW + s]); };
+  auto aready_bar = [&](int s) { return su32(&bars[2 * SX + 2 * SW + s]); };
+  auto afree_bar = [&](int s) { return su32(&bars[2 * SX + 2 * SW + AST + s]); };
+  constexpr int B8 = 2 * SX + 2 * SW + 2 * AST;
+  auto accf_bar = [&](int b) { return su32(&bars[B8 + b]); };
+  auto acce_bar = [&](int b) { return su32(&bars[B8 + 2 + b]); };
+  auto basef_bar = [&](int b) { return su32(&bars[B8 + 4 + b]); };
+  auto basee_bar = [&](int b) { return su32(&bars[B8 + 6 + b]); };
+  int* sbase = reinterpret_cast<int*>(bars + C::NBAR);                 // [2][128] row base exponents
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sbase + 2 * kSkRows);
+  unsigned* s_ticket = tmem_slot + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long it0 = (long long)blockIdx.x * a.T / a.G;
+  const long long it1 = (long long)(blockIdx.x + 1) * a.T / a.G;
+  const int niter = (int)(it1 - it0);
+  const int KS = a.KS;
+  unsigned* fault = &g_sk_fault;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < SX; ++s) { mbar_init(fullx_bar(s), 1); mbar_init(emptyx_bar(s), 1); }
+    for (int s = 0; s < SW; ++s) { mbar_init(fullw_bar(s), 1); mbar_init(emptyw_bar(s), kSkDqWarps); }
+    for (int s = 0; s < AST; ++s) { mbar_init(aready_bar(s), kSkDqWarps); mbar_init(afree_bar(s), 1); }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(accf_bar(b), 1);
+      mbar_init(acce_bar(b), kSkEpiWarps);
+      mbar_init(basef_bar(b), kSkEpiWarps);
+      mbar_init(basee_bar(b), kSkDqWarps);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == kSkMmaWarp) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_slot)),
+                 "r"(512u));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem_a = tmem + 2u * BN;
+  bool ok = true;
+
+  if (warp == kSkXProd) {
+    // ------------------------------ X producer --------------------------------
+    if (lane == 0) {
+      asm volatile("griddepcontrol.wait;" ::: "memory");  // X prepared by the previous grid
+      int tile = (int)(it0 / KS), ks = (int)(it0 % KS);
+      for (int i = 0; i < niter; ++i) {
+        const int s = i % SX;
+        if (i >= SX) ok = mbar_wait_flag(emptyx_bar(s), ((i / SX) + 1) & 1, fault);
+        if (!ok) break;
+        const uint8_t* src = a.xsw + ((size_t)(tile / a.tiles_n) * KS + ks) * (size_t)C::X_STAGE;
+        mbar_expect_tx(fullx_bar(s), (uint32_t)C::X_STAGE);
+        asm volatile(
+            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+            ::"r"(X_addr(s)), "l"(src), "r"((uint32_t)C::X_STAGE), "r"(fullx_bar(s))
+            : "memory");
+        if (++ks == KS) { ks = 0; ++tile; }
+      }
+    }
+  } else if (warp < kSkWProd0 + kSkWProds) {
+    // ------------------------------ W producers -------------------------------
+    if (lane == 0) {
+      const int p = warp - kSkWProd0;
+      for (int i = p; i < niter; i += kSkWProds) {
+        const int s = i % SW;
+        if (i >= SW) ok = mbar_wait_flag(emptyw_bar(s), ((i / SW) + 1) & 1, fault);
+        if (!ok) break;
+        const long long it = it0 + i;
+        const int tile = (int)(it / KS), ks = (int)(it % KS);
+        mbar_expect_tx(fullw_bar(s), (uint32_t)C::W_STAGE);
+        tma_load_2d(base + (uint32_t)W_off(s), &map_w, ks * (kSkBK / 2), (tile % a.tiles_n) * kSkRows, fullw_bar(s));
+      }
+    }
+  } else if (warp == kSkMmaWarp) {
+    // ------------------------------ MMA issuer --------------------------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(kSkRows, BN);
+      int kt = (int)(it0 % KS), seg = 0;
+      for (int i = 0; i < niter; ++i) {
+        const int sx = i % SX, sa = i % AST;
+        const bool first = (i == 0) || (kt == 0);
+        const bool last = (i == niter - 1) || (kt == KS - 1);
+        if (first && i > 0) ++seg;
+        const int b = seg & 1;
+        if (first && seg >= 2) ok = mbar_wait_flag(acce_bar(b), ((seg >> 1) + 1) & 1, fault);
+        ok = ok && mbar_wait_flag(aready_bar(sa), (i / AST) & 1, fault) &&
+             mbar_wait_flag(fullx_bar(sx), (i / SX) & 1, fault);
+        if (!ok) break;
+        tc_fence_after();
+        const uint64_t d0 = sw128_desc(X_addr(sx));
+        const uint32_t ta = tmem_a + (uint32_t)(sa * 128), td = tmem + (uint32_t)(b * BN);
+#pragma unroll
+        for (int kk = 0; kk < kSkBK / 16; ++kk)  // A: 8 TMEM columns per K=16; B: sub-tile kk/4, +32 bytes per K=16
+          umma_f16_ts(td, ta + (uint32_t)(kk * 8), d0 + (uint64_t)((kk >> 2) * (C::XBOX >> 4) + 2 * (kk & 3)),
+                      idesc, (!first || kk > 0) ? 1u : 0u);
+        umma_commit(emptyx_bar(sx));
+        umma_commit(afree_bar(sa));
+        if (last) umma_commit(accf_bar(b));
+        if (++kt == KS) kt = 0;
+      }
+    }
+  } else if (warp < kSkEpiWarp0) {
+    // ------------------------------ dequant -----------------------------------
+    const int q = warp & 3;                  // TMEM lane quadrant
+    const int j = (warp - kSkDqWarp0) >> 2;  // 64-k slice of the step
+    const int r = 32 * q + lane;             // weight row in the tile = TMEM lane
+    const uint32_t t_lane = (uint32_t)(32 * q) << 16;
+    // SWIZZLE_128B: 16-byte chunk c of 128-byte row r sits at chunk c ^ (r % 8)
+    const uint32_t w_c0 = (uint32_t)(r * 128 + (((2 * j) ^ (r & 7)) << 4));
+    const uint32_t w_c1 = (uint32_t)(r * 128 + (((2 * j + 1) ^ (r & 7)) << 4));
+    // Scale bits of this thread's 64 k (MXFP4 two E8M0 bytes, NVFP4 four E4M3
+    // bytes), loaded kSkScaleAhead steps ahead into a register ring.  Every
+    // load reads a valid address (rows past N and steps past the range are
+    // clamped: TMA zero-fills those rows' codes, so their factors never reach
+    // a stored output), so no select waits on a load in flight.
+    const size_t srow = (FMT == 0) ? (size_t)a.K / 32 : (size_t)a.K / 16;
+    const uint8_t* sc_col = a.scales + (FMT == 0 ? 2 * j : 4 * j);
+    int p_tile = (int)(it0 / KS), p_k = (int)(it0 % KS);
+    const uint8_t* p_row = nullptr;
+    auto row_ptr = [&](int t) {
+      int n = (t % a.tiles_n) * kSkRows + r;
+      n = n < a.N ? n : a.N - 1;
+      return sc_col + (size_t)n * srow;
+    };
+    p_row = row_ptr(p_tile);
+    auto next_scale = [&]() -> uint32_t {  // scale bits of step (p_tile, p_k), then advance (clamped at the end)
+      const uint32_t v = (FMT == 0) ? (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(p_row + p_k * 8))
+                                    : __ldg(reinterpret_cast<const uint32_t*>(p_row + p_k * 16));
+      const long long cur = (long long)p_tile * KS + p_k;
+      if (cur + 1 < it1) {
+        if (++p_k == KS) { p_k = 0; ++p_tile; p_row = row_ptr(p_tile); }
+      }
+      return v;
+    };
+    uint32_t ring[kSkScaleAhead];
+#pragma unroll
+    for (int u = 0; u < kSkScaleAhead; ++u) ring[u] = next_scale();
+    // 32 codes -> 16 f16x2 words with their block factors applied
+    auto widen = [&](uint4 pk4, uint32_t f_lo, uint32_t f_hi, uint32_t (&o)[16]) {
+      e2m1x8_to_f16x2(pk4.x, o);
+      e2m1x8_to_f16x2(pk4.y, o + 4);
+      e2m1x8_to_f16x2(pk4.z, o + 8);
+      e2m1x8_to_f16x2(pk4.w, o + 12);
+#pragma unroll
+      for (int u = 0; u < 16; ++u) o[u] = hmul2_f16x2(o[u], u < 8 ? f_lo : f_hi);
+    };
+    int kt = (int)(it0 % KS), seg = 0, rb = 0;
+    for (int i = 0; i < niter; ++i) {
+      const bool first = (i == 0) || (kt == 0);
+      if (first && i > 0) ++seg;
+      if (FMT == 0 && first) {
+        const int b = seg & 1;
+        ok = mbar_wait_flag(basef_bar(b), (seg >> 1) & 1, fault);
+        ok = __all_sync(0xFFFFFFFFu, ok);
+        if (!ok) break;
+        rb = sbase[b * kSkRows + r];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(basee_bar(b));
+      }
+      const int sw = i % SW, sa = i % AST;
+      const uint32_t sc = ring[0];
+#pragma unroll
+      for (int u = 0; u + 1 < kSkScaleAhead; ++u) ring[u] = ring[u + 1];
+      ring[kSkScaleAhead - 1] = next_scale();
+      uint32_t f0, f1, f2, f3;  // factors of the four 16-code halves of the two chunks
+      if (FMT == 0) {
+        const uint32_t b0 = sc & 0xFFu, b1 = (sc >> 8) & 0xFFu;
+        f0 = f1 = (b0 == 0xFFu) ? 0x7E007E00u : f16x2_pow2((int)b0 - 127 - rb);
+        f2 = f3 = (b1 == 0xFFu) ? 0x7E007E00u : f16x2_pow2((int)b1 - 127 - rb);
+      } else {
+        f0 = f16x2_e4m3(sc & 0xFFu); f1 = f16x2_e4m3((sc >> 8) & 0xFFu);
+        f2 = f16x2_e4m3((sc >> 16) & 0xFFu); f3 = f16x2_e4m3(sc >> 24);
+      }
+
+      ok = mbar_wait_flag(fullw_bar(sw), (i / SW) & 1, fault);
+      ok = __all_sync(0xFFFFFFFFu, ok);
+      if (!ok) break;
+      const uint4 c0 = *reinterpret_cast<const uint4*>(gbase + W_off(sw) + w_c0);
+      const uint4 c1 = *reinterpret_cast<const uint4*>(gbase + W_off(sw) + w_c1);
+      uint32_t o0[16], o1[16];
+      widen(c0, f0, f1, o0);
+      widen(c1, f2, f3, o1);
+      __syncwarp();                                   // every lane's codes are in registers:
+      if (lane == 0) mbar_arrive(emptyw_bar(sw));     // the W stage may be refilled
+      if (i >= AST) ok = mbar_wait_flag(afree_bar(sa), ((i / AST) + 1) & 1, fault);
+      ok = __all_sync(0xFFFFFFFFu, ok);
+      if (!ok) break;
+      tmem_st16(tmem_a + t_lane + (uint32_t)(sa * 128 + 32 * j), o0);
+      tmem_st16(tmem_a + t_lane + (uint32_t)(sa * 128 + 32 * j + 16), o1);
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(aready_bar(sa));
+      if (++kt == KS) kt = 0;
+    }
+  } else {
+    // ------------------------------ epilogue ----------------------------------
+    const int q = warp & 3;
+    const int r = 32 * q + lane;
+    const uint32_t t_lane = (uint32_t)(32 * q) << 16;
+    const int first_tile = (int)(it0 / KS);
+    // row factor exponent of a segment (MXFP4), or an L2 prefetch of its scales (NVFP4)
+    auto prepare = [&](long long it) -> int {
+      const int t = (int)(it / KS), kb = (int)(it % KS);
+      const int ke = (int)((kb + (it1 - it)) < KS ? (kb + (it1 - it)) : KS);
+      const int n = (t % a.tiles_n) * kSkRows + r;
+      if (n >= a.N) return 0;
+      if (FMT == 0) {
+        const int m = e8m0_row_max(a.scales + (size_t)n * (a.K / 32) + (size_t)kb * (kSkBK / 32),
+                                   (ke - kb) * (kSkBK / 32));
+        return m - 127 - 13;
+      }
+      const uint8_t* p = a.scales + (size_t)n * (a.K / 16) + (size_t)kb * (kSkBK / 16);
+      for (int off = 0; off < (ke - kb) * (kSkBK / 16); off += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(p + off));
+      return 0;
+    };
+    auto publish = [&](int b, int v) {
+      sbase[b * kSkRows + r] = v;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(basef_bar(b));
+    };
+    int rb_cur = 0;
+    if (niter > 0) {
+      rb_cur = prepare(it0);
+      if (FMT == 0) publish(0, rb_cur);
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // xs written by the X-preparation grid
+    long long it = it0;
+    for (int seg = 0; it < it1; ++seg) {
+      const int tile = (int)(it / KS), kb = (int)(it % KS);
+      const int ke = (int)((kb + (it1 - it)) < KS ? (kb + (it1 - it)) : KS);
+      const long long it_next = it + (ke - kb);
+      int rb_next = 0;
+      if (it_next < it1) {  // next segment's row bases while this one computes
+        const int b2 = (seg + 1) & 1;
+        if (FMT == 0 && seg + 1 >= 2) ok = ok && mbar_wait_flag(basee_bar(b2), (((seg + 1) >> 1) + 1) & 1, fault);
+        rb_next = prepare(it_next);
+        if (FMT == 0) publish(b2, rb_next);
+      }
+      const int b = seg & 1;
+      ok = ok && mbar_wait_flag(accf_bar(b), (seg >> 1) & 1, fault);
+      ok = __all_sync(0xFFFFFFFFu, ok);
+      tc_fence_after();
+      const int n = (tile % a.tiles_n) * kSkRows + r, m0 = (tile / a.tiles_n) * BN;
+      const bool live = n < a.N;
+      const float rowf = (FMT == 0) ? ldexpf(1.0f, rb_cur) : a.ts;
+      const bool whole = (kb == 0 && ke == KS);
+      const uint32_t tacc = tmem + t_lane + (uint32_t)(b * BN);
+      const int slot = 2 * (int)blockIdx.x + (tile == first_tile ? 0 : 1);
+      float* part = a.partials + (size_t)slot * (kSkRows * BN) + (size_t)r * BN;
+      if (ok) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          uint32_t v[16];
+          tmem_ld16(tacc + (uint32_t)c0, v);
+          if (whole) {
+            if (live) {
+#pragma unroll
+              for (int u = 0; u < 16; ++u) {
+                const int m = m0 + c0 + u;
+                if (m < a.M) {
+                  const float y = u2f(v[u]) * rowf * __ldg(a.xs + m);
+                  if (F32OUT) static_cast<float*>(a.Y)[(size_t)m * a.N + n] = y;
+                  else static_cast<__nv_bfloat16*>(a.Y)[(size_t)m * a.N + n] = __float2bfloat16_rn(y);
+                }
+              }
+            }
+          } else {
+#pragma unroll
+            for (int u = 0; u < 16; u += 4)
+              __stcg(reinterpret_cast<float4*>(part + c0 + u),
+                     make_float4(u2f(v[u]) * rowf, u2f(v[u + 1]) * rowf, u2f(v[u + 2]) * rowf,
+                                 u2f(v[u + 3]) * rowf));
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acce_bar(b));  // accumulator buffer free for segment seg + 2
+      if (!whole) {
+        // every epilogue warp takes the same named-barrier steps, also after a timeout
+        __threadfence();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (warp == kSkEpiWarp0 && lane == 0) *s_ticket = ok ? atomicAdd(a.counters + tile, 1u) : 0xFFFFFFFFu;
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        const unsigned ticket = *s_ticket;
+        const long long t0 = (long long)tile * KS, t1 = t0 + KS - 1;
+        const int c_lo = (int)(((t0 + 1) * a.G - 1) / a.T), c_hi = (int)(((t1 + 1) * a.G - 1) / a.T);
+        if (ticket == (unsigned)(c_hi - c_lo)) {  // last contributor: sum in CTA order
+          __threadfence();
+#pragma unroll 1
+          for (int c0 = 0; c0 < BN; c0 += 16) {
+            float acc[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) acc[u] = 0.0f;
+#pragma unroll 1
+            for (int cc = c_lo; cc <= c_hi; ++cc) {
+              const int cs = 2 * cc + (tile == (int)(((long long)cc * a.T / a.G) / KS) ? 0 : 1);
+              const float4* src = reinterpret_cast<const float4*>(a.partials + (size_t)cs * (kSkRows * BN) +
+                                                                  (size_t)r * BN + c0);
+              float4 pv[4];
+#pragma unroll
+              for (int u = 0; u < 4; ++u) pv[u] = __ldcg(src + u);
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                acc[4 * u] += pv[u].x; acc[4 * u + 1] += pv[u].y; acc[4 * u + 2] += pv[u].z; acc[4 * u + 3] += pv[u].w;
+              }
+            }
+            if (live) {
+#pragma unroll
+              for (int u = 0; u < 16; ++u) {
+                const int m = m0 + c0 + u;
+                if (m < a.M) {
+                  const float y = acc[u] * __ldg(a.xs + m);
+                  if (F32OUT) static_cast<float*>(a.Y)[(size_t)m * a.N + n] = y;
+                  else static_cast<__nv_bfloat16*>(a.Y)[(size_t)m * a.N + n] = __float2bfloat16_rn(y);
+                }
+              }
+            }
+          }
+          if (warp == kSkEpiWarp0 && lane == 0) a.counters[tile] = 0u;  // leave the workspace zeroed
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // s_ticket is reused by the next segment
+      }
+      rb_cur = rb_next;
+      it = it_next;
+    }
+  }
+
+  if (!ok) {
+    atomicExch(fault, 1u);
+    if (threadIdx.x == 0) {  // give copies and MMAs in flight a bounded chance to land
+      const unsigned long long t0 = gtimer();
+      while (gtimer() - t0 < 50000000ull) { }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kSkMmaWarp) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512u));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+bool make_tma_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr, uint64_t inner, uint64_t outer,
+                     uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw);
+
+int umma_sk_bn(int M) { return M >= 64 ? 64 : 32; }
+
+bool umma_sk_supported(const qgemm_weights_t* w, int M) {
+  return M >= 32 && M < 128 && (w->format == QGEMM_FMT_MXFP4 || w->format == QGEMM_FMT_NVFP4) &&
+         w->K % kSkBK == 0 && w->K <= (size_t)INT32_MAX && w->N <= (size_t)INT32_MAX &&
+         (reinterpret_cast<uintptr_t>(w->scales) & 3u) == 0;
+}
+
+struct SkPlan {
+  int bn, tiles_n, tiles, KS, G;
+  long long T;
+  size_t counter_bytes, partial_bytes;
+};
+
+static SkPlan sk_plan(const qgemm_weights_t* w, int M, int sm_count) {
+  SkPlan p;
+  p.bn = umma_sk_bn(M);
+  p.tiles_n = (int)((w->N + kSkRows - 1) / kSkRows);
+  p.tiles = p.tiles_n * ((M + p.bn - 1) / p.bn);
+  p.KS = (int)(w->K / kSkBK);
+  p.T = (long long)p.tiles * p.KS;
+  p.G = (int)(p.T < sm_count ? p.T : sm_count);
+  p.counter_bytes = ((size_t)p.tiles * sizeof(unsigned) + 255) & ~(size_t)255;
+  p.partial_bytes = (size_t)2 * p.G * kSkRows * p.bn * sizeof(float);
+  return p;
+}
+
+size_t umma_sk_workspace(const qgemm_weights_t* w, int M, int sm_count) {
+  const SkPlan p = sk_plan(w, M, sm_count);
+  return p.counter_bytes + p.partial_bytes;
+}
+
+template <int FMT, int BN, bool F32>
+static cudaError_t launch_sk_t(const CUtensorMap& mw, const SkArgs& a, cudaStream_t s) {
+  constexpr int BYTES = SkCfg<BN>::BYTES;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr[dev]) {
+    e = cudaFuncSetAttribute(k_umma_sk<FMT, BN, F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, BYTES);
+    if (e != cudaSuccess) return e;
+    attr[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)a.G);
+  cfg.blockDim = dim3(kSkThreads);
+  cfg.dynamicSmemBytes = BYTES;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_umma_sk<FMT, BN, F32>, mw, a);
+}
+
+template <int FMT, bool F32>
+static cudaError_t launch_sk_bn(int bn, const CUtensorMap& mw, const SkArgs& a, cudaStream_t s) {
+  return bn == 32 ? launch_sk_t<FMT, 32, F32>(mw, a, s) : launch_sk_t<FMT, 64, F32>(mw, a, s);
+}
+
+// Xh / xs: the f16 copy of X in the swizzled operand layout and its row
+// factors (k_xprep with swz_bn = umma_sk_bn(M)); ws: the
+// counters + partials block of umma_sk_workspace bytes (counters zero).
+qgemm_status_t gemm_umma_sk(const qgemm_weights_t* w, const __half* Xh, const float* xs, int M, void* Y, bool f32,
+                            void* ws, int sm_count, cudaStream_t s) {
+  if (!umma_sk_supported(w, M)) return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "stream-K tcgen05 path: unsupported shape");
+  if (sm_count <= 0) return fail(QGEMM_ERR_CUDA, "stream-K tcgen05 path: no device properties");
+  const SkPlan p = sk_plan(w, M, sm_count);
+  CUtensorMap mw;
+  if (!make_tma_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->data, w->K / 2, w->N, w->K / 2, kSkBK / 2, kSkRows,
+                       CU_TENSOR_MAP_SWIZZLE_128B))
+    return fail(QGEMM_ERR_CUDA, "stream-K tcgen05 path: cuTensorMapEncodeTiled failed");
+  SkArgs a;
+  a.scales = static_cast<const uint8_t*>(w->scales);
+  a.xsw = reinterpret_cast<const uint8_t*>(Xh);
+  a.Y = Y; a.xs = xs;
+  a.counters = static_cast<unsigned*>(ws);
+  a.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + p.counter_bytes);
+  a.T = p.T; a.M = M; a.N = (int)w->N; a.K = (int)w->K;
+  a.tiles_n = p.tiles_n; a.KS = p.KS; a.G = p.G; a.ts = w->tensor_scale;
+  cudaError_t e;
+  if (w->format == QGEMM_FMT_MXFP4)
+    e = f32 ? launch_sk_bn<0, true>(p.bn, mw, a, s) : launch_sk_bn<0, false>(p.bn, mw, a, s);
+  else
+    e = f32 ? launch_sk_bn<1, true>(p.bn, mw, a, s) : launch_sk_bn<1, false>(p.bn, mw, a, s);
+  if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "stream-K tcgen05 launch: %s", cudaGetErrorString(e));
+  return QGEMM_OK;
+}
+
+unsigned umma_sk_fault() {
+  unsigned f = 0;
+  if (cudaMemcpyFromSymbol(&f, g_sk_fault, sizeof(f)) != cudaSuccess) return 0xFFFFFFFFu;
+  return f;
+}
+
+}  // namespace qg
