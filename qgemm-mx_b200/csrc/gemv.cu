@@ -49,6 +49,7 @@
 #include <cuda_fp16.h>
 
 #include "common.cuh"
+#include "gemv_core.cuh"
 
 namespace qg {
 
@@ -74,142 +75,39 @@ struct GemvArgs {
 };
 
 // ---------------------------------------------------------------------------
-// small PTX helpers
-// ---------------------------------------------------------------------------
-
-__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                        uint32_t b0, uint32_t b1) {
-  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-// d = A.B (accumulator starts at zero)
-__device__ __forceinline__ void mma_f16_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                          uint32_t b0, uint32_t b1) {
-  const float z = 0.0f;
-  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%10,%10,%10,%10};"
-      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
-}
-
-__device__ __forceinline__ uint4 ldg_stream16(const void* p) {  // read once: skip L1
-  uint4 v;
-  asm("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
-  return v;
-}
-__device__ __forceinline__ uint2 ldg_stream8(const void* p) {
-  uint2 v;
-  asm("ld.global.nc.L1::no_allocate.L2::256B.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
-  return v;
-}
-// 4-byte pieces of one 16-byte block: allocate in L1 so the 3 sibling loads
-// of the same sector hit there.
-__device__ __forceinline__ uint32_t ldg_first4(const void* p) {
-  uint32_t v;
-  asm("ld.global.nc.L1::evict_first.L2::256B.u32 %0, [%1];" : "=r"(v) : "l"(p));
-  return v;
-}
-__device__ __forceinline__ uint4 ldg_keep16(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
-
-// byte t of q (codes 2t, 2t+1) -> f16x2 (low half = even code)
-__device__ __forceinline__ void e2m1x8_to_f16(uint32_t q, uint32_t (&o)[4]) {
-  asm("{ .reg .b8 b0, b1, b2, b3;\n"
-      "  mov.b32 {b0, b1, b2, b3}, %4;\n"
-      "  cvt.rn.f16x2.e2m1x2 %0, b0;\n"
-      "  cvt.rn.f16x2.e2m1x2 %1, b1;\n"
-      "  cvt.rn.f16x2.e2m1x2 %2, b2;\n"
-      "  cvt.rn.f16x2.e2m1x2 %3, b3; }\n"
-      : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3])
-      : "r"(q));
-}
-
-__device__ __forceinline__ uint32_t hmul2_f16(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-
-// 8 INT4 codes -> f16x2 words (c0,c4) (c1,c5) (c2,c6) (c3,c7).  With
-// u = q ^ 0x8 (= value + 8), nibble u placed in the mantissa of f16 1024
-// gives 1024 + u, or 1024 + 16u when taken from the upper nibble of a byte;
-// one subtract / fused multiply-add recovers the signed value exactly.
-__device__ __forceinline__ void int4x8_to_f16(uint32_t q, uint32_t (&o)[4]) {
-  const uint32_t lo = q ^ 0x88888888u, hi = lo >> 8;
-  constexpr uint32_t MAGIC = 0x64006400u;
-  uint32_t w0, w1, w2, w3;
-  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(w0) : "r"(lo), "r"(0x000F000Fu), "r"(MAGIC));
-  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(w1) : "r"(lo), "r"(0x00F000F0u), "r"(MAGIC));
-  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(w2) : "r"(hi), "r"(0x000F000Fu), "r"(MAGIC));
-  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(w3) : "r"(hi), "r"(0x00F000F0u), "r"(MAGIC));
-  constexpr uint32_t SUB = 0x64086408u;    // 1032
-  constexpr uint32_t K16 = 0x2C002C00u;    // 1/16
-  constexpr uint32_t NEG72 = 0xD480D480u;  // -72
-  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(o[0]) : "r"(w0), "r"(SUB));
-  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(o[1]) : "r"(w1), "r"(K16), "r"(NEG72));
-  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(o[2]) : "r"(w2), "r"(SUB));
-  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(o[3]) : "r"(w3), "r"(K16), "r"(NEG72));
-}
-
-// True if any byte of v equals 0x00 or 0xFF (classic zero-byte test on v and ~v).
-__device__ __forceinline__ bool has_00_or_ff(uint32_t v) {
-  const uint32_t nv = ~v;
-  return (((v - 0x01010101u) & ~v) | ((nv - 0x01010101u) & ~nv)) & 0x80808080u;
-}
-
-// 2^(b-127) for an E8M0 byte b in 1..254 (callers route 0x00 / 0xFF through
-// the exact e8m0_decode).
-__device__ __forceinline__ float e8m0_fast(uint32_t word, int byte) {
-  return u2f(((word >> (8 * byte)) & 0xFFu) << 23);
-}
-
-// f16x2 broadcast of each of the two E4M3 bytes in the low half of v, exact
-// for normal E4M3 codes (exponent field 1..15, not the NaN code): f16 keeps
-// the sign, rebiases the exponent by +8 and widens the mantissa.  Returns
-// false when either byte is zero, subnormal or NaN (callers then use the
-// exact path).
-__device__ __forceinline__ bool e4m3x2_to_f16x2_fast(uint32_t v, uint32_t& lo, uint32_t& hi) {
-  const uint32_t e0 = (v >> 3) & 0xFu, e1 = (v >> 11) & 0xFu;
-  const uint32_t m0 = v & 0x7Fu, m1 = (v >> 8) & 0x7Fu;
-  const bool ok = e0 != 0 && e1 != 0 && m0 != 0x7Fu && m1 != 0x7Fu;
-  const uint32_t h0 = ((v & 0x80u) << 8) | ((m0 << 7) + 0x2000u);
-  const uint32_t h1 = ((v & 0x8000u)) | ((m1 << 7) + 0x2000u);
-  lo = h0 | (h0 << 16);
-  hi = h1 | (h1 << 16);
-  return ok;
-}
-
-__device__ __forceinline__ uint32_t f16x2_of(float f) {
-  const uint32_t h = (uint32_t)__half_as_ushort(__float2half_rn(f));  // exact for e4m3 values
-  return h | (h << 16);
-}
-
-// ---------------------------------------------------------------------------
 // X preparation
 // ---------------------------------------------------------------------------
 
 // One CTA per activation row.  For INT4 formats the f16 values of each group
 // of 8 are stored in the order (x0,x4,x1,x5,x2,x6,x3,x7) to match the
 // (c_i, c_i+4) pairs that int4x8_to_f16 produces.
-// swz_bn > 0 selects the tcgen05 operand layout instead: for each block of
-// swz_bn activation rows and each 64-k block, swz_bn rows of 128 bytes whose
-// 16-byte chunk c is stored at chunk c ^ (row % 8) -- the shared-memory image
-// of a 128-byte-swizzled K-major tile, so one linear bulk copy stages it.
-// Rows M .. ceil(M / swz_bn) * swz_bn - 1 (one CTA each) are written as zeros.
-__device__ __forceinline__ size_t xprep_index(int m, int k, int K, int swz_bn) {
-  if (swz_bn == 0) return (size_t)m * K + k;
-  const int mb = m / swz_bn, r = m % swz_bn, kb = k >> 6, c = (k >> 3) & 7;
-  return (((size_t)mb * (K >> 6) + kb) * swz_bn + r) * 64 + (size_t)((c ^ (r & 7)) << 3);
+// Output layouts (lp = layout parameter):
+//  0  row-major [M][K].
+//  1  tcgen05 operand image (lp = BN): for each block of BN activation rows
+//     and each 64-k block, BN rows of 128 bytes whose 16-byte chunk c is
+//     stored at chunk c ^ (row % 8) -- the shared-memory image of a
+//     128-byte-swizzled K-major tile, so one linear bulk copy stages it.
+//  2  TMA decode image (lp = mpad rows): for each 256-k unit, mpad rows of 32
+//     16-byte chunks, chunk c of row m at (c & ~7) | ((c ^ m) & 7), so the
+//     warp-MMA fragment loads from shared memory are free of bank conflicts.
+// Rows M .. (padded row count) - 1 (one CTA each) are written as zeros.
+__device__ __forceinline__ size_t xprep_index(int m, int k, int K, int layout, int lp) {
+  if (layout == 0) return (size_t)m * K + k;
+  if (layout == 1) {
+    const int mb = m / lp, r = m % lp, kb = k >> 6, c = (k >> 3) & 7;
+    return (((size_t)mb * (K >> 6) + kb) * lp + r) * 64 + (size_t)((c ^ (r & 7)) << 3);
+  }
+  const int u = k >> 8, c = (k >> 3) & 31;
+  const int pos = (c & ~7) | ((c ^ m) & 7);
+  return (((size_t)u * lp + m) * 32 + pos) * 8;
 }
-__global__ void __launch_bounds__(256) k_xprep(const uint16_t* __restrict__ X, int M, int K, int perm, int swz_bn,
-                                               __half* __restrict__ Xh, float* __restrict__ xs) {
+__global__ void __launch_bounds__(256) k_xprep(const uint16_t* __restrict__ X, int M, int K, int perm, int layout,
+                                               int lp, __half* __restrict__ Xh, float* __restrict__ xs) {
   asm volatile("griddepcontrol.launch_dependents;");
   const int m = blockIdx.x;
   if (m >= M) {  // zero padding rows of the last activation block
     for (int k = threadIdx.x * 8; k < K; k += blockDim.x * 8)
-      *reinterpret_cast<uint4*>(Xh + xprep_index(m, k, K, swz_bn)) = make_uint4(0u, 0u, 0u, 0u);
+      *reinterpret_cast<uint4*>(Xh + xprep_index(m, k, K, layout, lp)) = make_uint4(0u, 0u, 0u, 0u);
     return;
   }
   __shared__ float red[8];
@@ -259,7 +157,7 @@ __global__ void __launch_bounds__(256) k_xprep(const uint16_t* __restrict__ X, i
 #pragma unroll
       for (int i = 0; i < 4; ++i) o[i] = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
     }
-    *reinterpret_cast<uint4*>(Xh + xprep_index(m, k, K, swz_bn)) = *reinterpret_cast<const uint4*>(o);
+    *reinterpret_cast<uint4*>(Xh + xprep_index(m, k, K, layout, lp)) = *reinterpret_cast<const uint4*>(o);
   }
 }
 
@@ -463,114 +361,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) k_gemv(const GemvArgs a) {
       for (int q = 0; q < 16; ++q) cx[t][q] = xf[t][q];
     if (it + 1 < end) { load_w(ntile, nc); load_x(nc); }
 
-    if constexpr (FMT == 0) {
-      // block b of the chunk = MMAs (b,0), (b,1); post-scale by 2^(e8m0-127)
-      bool special[R];
-#pragma unroll
-      for (int r = 0; r < R; ++r) special[r] = has_00_or_ff(cs[r][0]) || has_00_or_ff(cs[r][1]);
-#pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        uint32_t A[R][2][4];
-#pragma unroll
-        for (int r = 0; r < R; ++r)
-#pragma unroll
-          for (int h = 0; h < 2; ++h) e2m1x8_to_f16(cw[r][h][b], A[r][h]);
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-          float s0 = e8m0_fast(cs[r][0], b), s1 = e8m0_fast(cs[r][1], b);
-          if (special[r]) {  // a 0x00 (2^-127) or 0xFF (NaN) scale in this chunk
-            s0 = e8m0_decode(cs[r][0] >> (8 * b));
-            s1 = e8m0_decode(cs[r][1] >> (8 * b));
-          }
-#pragma unroll
-          for (int t = 0; t < NT; ++t) {
-            float tmp[4];
-            mma_f16_z(tmp, A[r][0][0], A[r][1][0], A[r][0][1], A[r][1][1], cx[t][4 * b + 0], cx[t][4 * b + 1]);
-            mma_f16(tmp, A[r][0][2], A[r][1][2], A[r][0][3], A[r][1][3], cx[t][4 * b + 2], cx[t][4 * b + 3]);
-            acc[r][t][0] = fmaf(s0, tmp[0], acc[r][t][0]);
-            acc[r][t][1] = fmaf(s0, tmp[1], acc[r][t][1]);
-            acc[r][t][2] = fmaf(s1, tmp[2], acc[r][t][2]);
-            acc[r][t][3] = fmaf(s1, tmp[3], acc[r][t][3]);
-          }
-        }
-      }
-    } else if constexpr (FMT == 1) {
-      // words 0,1 -> block 2j, words 2,3 -> block 2j+1; fold e4m3 into f16
-      uint32_t sw[R][2][2];
-#pragma unroll
-      for (int r = 0; r < R; ++r)
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-          if (!e4m3x2_to_f16x2_fast(cs[r][h], sw[r][h][0], sw[r][h][1])) {
-            sw[r][h][0] = f16x2_of(e4m3_decode(cs[r][h] & 0xFFu));
-            sw[r][h][1] = f16x2_of(e4m3_decode((cs[r][h] >> 8) & 0xFFu));
-          }
-#pragma unroll
-      for (int qw = 0; qw < 4; ++qw) {
-        uint32_t A[R][2][4];
-#pragma unroll
-        for (int r = 0; r < R; ++r)
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            e2m1x8_to_f16(cw[r][h][qw], A[r][h]);
-            const uint32_t m2 = sw[r][h][qw >> 1];
-#pragma unroll
-            for (int p = 0; p < 4; ++p) A[r][h][p] = hmul2_f16(A[r][h][p], m2);
-          }
-#pragma unroll
-        for (int s = 0; s < 2; ++s) {
-          const int i = 2 * qw + s;
-#pragma unroll
-          for (int r = 0; r < R; ++r)
-#pragma unroll
-            for (int t = 0; t < NT; ++t)
-              mma_f16(acc[r][t], A[r][0][2 * s], A[r][1][2 * s], A[r][0][2 * s + 1], A[r][1][2 * s + 1],
-                      cx[t][2 * i], cx[t][2 * i + 1]);
-        }
-      }
-    } else {
-      // INT4: FP32 partial per group, post-scaled by the FP16 group scale
-      float tmp[R][NT][4];
-#pragma unroll
-      for (int qw = 0; qw < 4; ++qw) {
-        uint32_t A[R][2][4];
-#pragma unroll
-        for (int r = 0; r < R; ++r)
-#pragma unroll
-          for (int h = 0; h < 2; ++h) int4x8_to_f16(cw[r][h][qw], A[r][h]);
-#pragma unroll
-        for (int s = 0; s < 2; ++s) {
-          const int i = 2 * qw + s;
-          const bool first = (FMT == 2) ? (i == 0) : (i == 0 || i == 4);
-#pragma unroll
-          for (int r = 0; r < R; ++r)
-#pragma unroll
-            for (int t = 0; t < NT; ++t) {
-              if (first)
-                mma_f16_z(tmp[r][t], A[r][0][2 * s], A[r][1][2 * s], A[r][0][2 * s + 1], A[r][1][2 * s + 1],
-                          cx[t][2 * i], cx[t][2 * i + 1]);
-              else
-                mma_f16(tmp[r][t], A[r][0][2 * s], A[r][1][2 * s], A[r][0][2 * s + 1], A[r][1][2 * s + 1],
-                        cx[t][2 * i], cx[t][2 * i + 1]);
-            }
-        }
-        if ((FMT == 3 && qw == 1) || qw == 3) {  // end of a group
-          const int sh = (FMT == 3 && qw == 3) ? 16 : 0;
-#pragma unroll
-          for (int r = 0; r < R; ++r) {
-            const float s0 = __half2float(__ushort_as_half((unsigned short)((cs[r][0] >> sh) & 0xFFFFu)));
-            const float s1 = __half2float(__ushort_as_half((unsigned short)((cs[r][1] >> sh) & 0xFFFFu)));
-#pragma unroll
-            for (int t = 0; t < NT; ++t) {
-              acc[r][t][0] = fmaf(s0, tmp[r][t][0], acc[r][t][0]);
-              acc[r][t][1] = fmaf(s0, tmp[r][t][1], acc[r][t][1]);
-              acc[r][t][2] = fmaf(s1, tmp[r][t][2], acc[r][t][2]);
-              acc[r][t][3] = fmaf(s1, tmp[r][t][3], acc[r][t][3]);
-            }
-          }
-        }
-      }
-    }
+    chunk_mma<FMT, R, NT>(acc, cw, cs, cx);
 
     if (c == C - 1 || it + 1 == end) {
       flush(tile, seg_full_start && (c == C - 1));
@@ -700,6 +491,16 @@ size_t umma_sk_workspace(const qgemm_weights_t* w, int M, int sm_count);
 qgemm_status_t gemm_umma_sk(const qgemm_weights_t* w, const __half* Xh, const float* xs, int M, void* Y, bool f32,
                             void* ws, int sm_count, cudaStream_t s);
 
+bool gemv_tma_supported(const qgemm_weights_t* w, int mb);
+size_t gemv_tma_workspace(const qgemm_weights_t* w, int sm_count);
+size_t gemv_tma_xg_offset(const qgemm_weights_t* w, int sm_count);
+qgemm_status_t gemm_gemv_tma(const qgemm_weights_t* w, const __half* xg, const float* xs, int mb, void* Y, int ldy,
+                             bool f32, void* ws, int sm_count, cudaStream_t s);
+// [xs (16 floats) | counters | partials | X image]
+static size_t decode_tma_workspace(const qgemm_weights_t* w, int sms) {
+  return pad256((size_t)kMaxM * sizeof(float)) + gemv_tma_workspace(w, sms);
+}
+
 // The tcgen05 paths (dequantised W in TMEM) take MXFP4 / NVFP4 with M >= 32:
 // the persistent stream-K kernel for M < 256 and K % 128 == 0 (umma_sk.cu),
 // the tile-per-CTA kernel with K splits otherwise (K % 64 == 0, umma.cu).
@@ -755,13 +556,35 @@ qgemm_status_t gemm_decode(const qgemm_weights_t* w, const uint16_t* X, int M, v
     void* split_ws = static_cast<uint8_t*>(ws) + pad256((size_t)M * sizeof(float)) + umma_xh_bytes(w, M);
     if (umma_sk_supported(w, M)) {
       const int bn = umma_sk_bn(M);
-      k_xprep<<<(M + bn - 1) / bn * bn, 256, 0, s>>>(X, M, (int)w->K, 0, bn, xh, xs);
+      k_xprep<<<(M + bn - 1) / bn * bn, 256, 0, s>>>(X, M, (int)w->K, 0, 1, bn, xh, xs);
       QG_LAUNCH_RET();
       return gemm_umma_sk(w, xh, xs, M, Y, f32, split_ws, sm_count_or_zero(), s);
     }
-    k_xprep<<<M, 256, 0, s>>>(X, M, (int)w->K, 0, 0, xh, xs);
+    k_xprep<<<M, 256, 0, s>>>(X, M, (int)w->K, 0, 0, 0, xh, xs);
     QG_LAUNCH_RET();
     return gemm_umma_ts(w, xh, xs, M, Y, f32, umma_split_count(w, M), split_ws, s);
+  }
+  if (gemv_tma_supported(w, M < kMaxM ? M : kMaxM)) {
+    // TMA-fed decode kernel (gemv_tma.cu), one launch per 16 activation rows
+    const int sms = sm_count_or_zero();
+    const size_t need = decode_tma_workspace(w, sms);
+    if (sms <= 0 || !ws || !al16(ws) || ws_bytes < need)
+      return fail(QGEMM_ERR_WORKSPACE, "gemm: 16-byte aligned workspace of %zu bytes needed, %zu given", need,
+                  ws_bytes);
+    float* xs = static_cast<float*>(ws);
+    uint8_t* tws = static_cast<uint8_t*>(ws) + pad256((size_t)kMaxM * sizeof(float));
+    __half* xg = reinterpret_cast<__half*>(tws + gemv_tma_xg_offset(w, sms));
+    for (int m0 = 0; m0 < M; m0 += kMaxM) {
+      const int mb = (M - m0) < kMaxM ? (M - m0) : kMaxM;
+      const int mpad = mb <= 8 ? 8 : 16;
+      k_xprep<<<mpad, 256, 0, s>>>(X + (size_t)m0 * w->K, mb, (int)w->K, 0, 2, mpad, xg, xs);
+      QG_LAUNCH_RET();
+      void* Yb = f32 ? (void*)(static_cast<float*>(Y) + (size_t)m0 * w->N)
+                     : (void*)(static_cast<uint16_t*>(Y) + (size_t)m0 * w->N);
+      st = gemm_gemv_tma(w, xg, xs, mb, Yb, (int)w->N, f32, tws, sms, s);
+      if (st != QGEMM_OK) return st;
+    }
+    return QGEMM_OK;
   }
   if (!ws || !al16(ws) || ws_bytes < p.total())
     return fail(QGEMM_ERR_WORKSPACE, "gemm: 16-byte aligned workspace of %zu bytes needed, %zu given", p.total(),
@@ -784,7 +607,7 @@ qgemm_status_t gemm_decode(const qgemm_weights_t* w, const uint16_t* X, int M, v
     a.T = pb.T; a.C = pb.C; a.W_total = pb.W_total; a.M = mb;
     a.Y = f32 ? (void*)(static_cast<float*>(Y) + (size_t)m0 * w->N)
               : (void*)(static_cast<uint16_t*>(Y) + (size_t)m0 * w->N);
-    k_xprep<<<mb, 256, 0, s>>>(X + (size_t)m0 * w->K, mb, (int)w->K, perm, 0, xh, xs);
+    k_xprep<<<mb, 256, 0, s>>>(X + (size_t)m0 * w->K, mb, (int)w->K, perm, 0, 0, xh, xs);
     QG_LAUNCH_RET();
     const cudaError_t e = f32 ? launch_gemv<true>(pb, a, s) : launch_gemv<false>(pb, a, s);
     if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "gemm: launch failed: %s", cudaGetErrorString(e));
@@ -794,6 +617,10 @@ qgemm_status_t gemm_decode(const qgemm_weights_t* w, const uint16_t* X, int M, v
 
 size_t gemm_decode_workspace(const qgemm_weights_t* w, int M) {
   if (w && use_umma(w, M)) return umma_workspace(w, M);
+  if (w && M >= 1 && gemv_tma_supported(w, M < kMaxM ? M : kMaxM)) {
+    const int sms = sm_count_or_zero();
+    return sms > 0 ? decode_tma_workspace(w, sms) : 0;
+  }
   GemvPlan p;
   if (!w || M < 1 || gemv_plan(w, M < kMaxM ? M : kMaxM, &p) != QGEMM_OK) return 0;
   size_t need = p.total();
@@ -917,7 +744,7 @@ extern "C" qgemm_status_t qgemm_gemm_w4a16_noalloc(const qgemm_weights_t* w, con
     if (st != QGEMM_OK) return st;
     a.T = pb.T; a.C = pb.C; a.W_total = pb.W_total; a.M = mb;
     a.Y = static_cast<uint16_t*>(Y) + (size_t)m0 * w->N;
-    k_xprep<<<mb, 256, 0, s>>>(X + (size_t)m0 * w->K, mb, (int)w->K, perm, 0, xh, xs);
+    k_xprep<<<mb, 256, 0, s>>>(X + (size_t)m0 * w->K, mb, (int)w->K, perm, 0, 0, xh, xs);
     QG_LAUNCH_RET();
     const cudaError_t e = launch_gemv<false>(pb, a, s);
     if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "gemm_noalloc: launch failed: %s", cudaGetErrorString(e));

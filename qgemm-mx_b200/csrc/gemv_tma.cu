@@ -1,0 +1,446 @@
+// gemv_tma.cu -- TMA-fed decode GEMM for M <= 16 (MXFP4 / NVFP4, K % 256 == 0).
+//
+// Same arithmetic as k_gemv (gemv.cu, through chunk_mma in gemv_core.cuh):
+// swap-AB mma.sync m16n8k16 with f16 operands and FP32 accumulation, exact
+// E2M1 widening, MXFP4 block scales applied to FP32 per-block partial sums,
+// NVFP4 E4M3 scales folded into f16.  What changes is how the weight stream
+// reaches the warps.  k_gemv loads W straight into registers, which bounds
+// the bytes in flight per SM by the register file; here a persistent CTA per
+// SM keeps a deep shared-memory ring full with TMA, so HBM sees enough
+// requests in flight to run near its peak.
+//
+// Unit of work: a tile of 128 weight rows x 256 k (16 KB of packed codes).
+// Schedule: stream-K over (tile, 256-k unit), one contiguous range per CTA;
+// tiles split across CTAs are reduced through the workspace by the CTA whose
+// ticket shows it arrived last, summing contributors in CTA order.
+//
+// Warp roles (576 or 320 threads):
+//   warps 0, 1   producers, alternate units.  Lane 0 arms the stage's
+//                mbarrier and issues the packed-W box (TMA, 128 rows x 128 B,
+//                128-byte swizzle) and the unit's X tile (one linear bulk copy
+//                of the image k_xprep wrote, layout 2); all 32 lanes copy the
+//                unit's scale bytes with 4-byte cp.async and arrive on the
+//                same mbarrier when their copies land.  No multicast.
+//   warps 2..    consumers.  M <= 8: sixteen warps, warp (g, c) owns weight
+//                rows 16g .. 16g + 15 and 128-k chunk c of every unit; the
+//                pair's sums are added (chunk 0 + chunk 1) at each segment
+//                end.  M <= 16: eight warps, one per 16-row group, both chunks.
+//                Each runs chunk_mma on codes, scales and X fragments read
+//                from the stage.
+// Every mbarrier wait is bounded (tc.cuh); on timeout the kernel sets
+// g_gemv_tma_fault and returns after letting copies in flight land.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "gemv_core.cuh"
+#include "tc.cuh"
+
+namespace qg {
+
+__device__ unsigned g_gemv_tma_fault = 0;
+
+constexpr int kGtUnitK = 256;
+constexpr int kGtRows = 128;
+constexpr int kGtProd = 2;
+constexpr int kGtGroups = 8;   // 16-row groups per 128-row tile
+
+template <int FMT, int NT>
+struct GtCfg {
+  // consumers: one warp per (16-row group, 128-k chunk) when registers allow
+  // (NT = 1), else one warp per 16-row group covering both chunks
+  static constexpr int KSPLIT = NT == 1 ? 2 : 1;
+  static constexpr int CONS = kGtGroups * KSPLIT;
+  static constexpr int THREADS = 32 * (kGtProd + CONS);
+  static constexpr int MPAD = 8 * NT;
+  static constexpr int SB = (FMT == 0) ? kGtUnitK / 32 : kGtUnitK / 16;   // scale bytes per row per unit
+  static constexpr int W_BYTES = kGtRows * kGtUnitK / 2;                // 16 KB
+  static constexpr int X_BYTES = MPAD * kGtUnitK * 2;
+  static constexpr int S_BYTES = kGtRows * SB;
+  static constexpr int STAGE = ((W_BYTES + X_BYTES + S_BYTES) + 1023) / 1024 * 1024;
+  static constexpr int STAGES = ((200 * 1024) / STAGE) & ~1;            // even: two producers
+  static constexpr int BYTES = 1024 + STAGES * STAGE + 2 * STAGES * 8 + 16 + (KSPLIT - 1) * kGtGroups * NT * 32 * 16;
+  static_assert(BYTES <= 232448, "shared memory");
+  static_assert(STAGES >= 4, "ring depth");
+};
+
+struct GtArgs {
+  const uint8_t* scales;
+  const uint8_t* xg;     // X in layout 2 of k_xprep: [K/256][mpad][32 chunks], chunk c at (c & ~7) | ((c ^ m) & 7)
+  const float* xs;
+  void* Y;
+  float* partials;       // [2 * G][8 row groups][NT][32 lanes] float4
+  unsigned* counters;    // [tiles]
+  long long T;           // tiles * KS
+  int M, N, K, ldy;
+  int KS;                // units per tile (K / 256)
+  int G;
+  float ts;
+};
+
+template <int FMT, int NT, bool F32OUT>
+__global__ void __launch_bounds__(GtCfg<FMT, NT>::THREADS, 1)
+k_gemv_tma(const __grid_constant__ CUtensorMap map_w, const GtArgs a) {
+  using C = GtCfg<FMT, NT>;
+  constexpr int kGtCons = C::CONS;
+  constexpr int S = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = su32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  // stage s: [W 128 x 128 B (swizzled) | X mpad x 512 B | scales 128 x SB]
+  auto W_off = [&](int s) { return s * C::STAGE; };
+  auto X_off = [&](int s) { return s * C::STAGE + C::W_BYTES; };
+  auto S_off = [&](int s) { return s * C::STAGE + C::W_BYTES + C::X_BYTES; };
+  uint64_t* bars = reinterpret_cast<uint64_t*>(gbase + S * C::STAGE);
+  auto full_bar = [&](int s) { return su32(&bars[s]); };
+  auto empty_bar = [&](int s) { return su32(&bars[S + s]); };
+  unsigned* s_ticket = reinterpret_cast<unsigned*>(bars + 2 * S);
+  float4* s_half = reinterpret_cast<float4*>(bars + 2 * S + 2);  // [8 groups][NT][32]: chunk-1 sums
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long it0 = (long long)blockIdx.x * a.T / a.G;
+  const long long it1 = (long long)(blockIdx.x + 1) * a.T / a.G;
+  const int niter = (int)(it1 - it0);
+  const int KS = a.KS;
+  unsigned* fault = &g_gemv_tma_fault;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full_bar(s), 1 + 32);   // lane 0's expect_tx arrival + 32 cp.async arrivals
+      mbar_init(empty_bar(s), kGtCons);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  bool ok = true;
+
+  if (warp < kGtProd) {
+    // ------------------------------ producers ---------------------------------
+    const int p = warp;
+    const size_t srow = (size_t)a.K / (FMT == 0 ? 32 : 16);
+    auto issue_wx = [&](int i, bool with_w, bool with_x) {
+      const int s = i % S;
+      const long long it = it0 + i;
+      const int tile = (int)(it / KS), ks = (int)(it % KS);
+      if (with_w) {
+        mbar_expect_tx(full_bar(s), (uint32_t)(C::W_BYTES + C::X_BYTES));
+        tma_load_2d(base + (uint32_t)W_off(s), &map_w, ks * (kGtUnitK / 2), tile * kGtRows, full_bar(s));
+      }
+      if (with_x) {
+        const uint8_t* src = a.xg + (size_t)ks * C::X_BYTES;
+        asm volatile(
+            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+            ::"r"(base + (uint32_t)X_off(s)), "l"(src), "r"((uint32_t)C::X_BYTES), "r"(full_bar(s))
+            : "memory");
+      }
+    };
+    auto issue_scales = [&](int i) {
+      const int s = i % S;
+      const long long it = it0 + i;
+      const int tile = (int)(it / KS), ks = (int)(it % KS);
+      constexpr int WPR = C::SB / 4;  // 4-byte words per row
+#pragma unroll
+      for (int e = lane; e < kGtRows * WPR; e += 32) {
+        const int row = e / WPR, wi = e % WPR;
+        int n = tile * kGtRows + row;
+        n = n < a.N ? n : a.N - 1;  // rows past N: TMA zero-fills their codes
+        const uint8_t* src = a.scales + (size_t)n * srow + (size_t)ks * C::SB + 4 * wi;
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(base + (uint32_t)(S_off(s) + row * C::SB + 4 * wi)),
+                     "l"(src) : "memory");
+      }
+      asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(full_bar(s)) : "memory");
+    };
+    const int pre = niter < S ? niter : S;
+    // Weights and scales do not depend on the X-preparation grid: start them first.
+    for (int i = p; i < pre; i += kGtProd) {
+      if (lane == 0) issue_wx(i, true, false);
+      issue_scales(i);
+    }
+    if (lane == 0) {
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      for (int i = p; i < pre; i += kGtProd) issue_wx(i, false, true);
+    }
+    for (int i = pre + ((p - pre % kGtProd + kGtProd) % kGtProd); i < niter; i += kGtProd) {
+      const int s = i % S;
+      if (lane == 0) ok = mbar_wait_flag(empty_bar(s), ((i / S) + 1) & 1, fault);
+      ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+      if (!ok) break;
+      if (lane == 0) issue_wx(i, true, true);
+      issue_scales(i);
+    }
+  } else {
+    // ------------------------------ consumers ---------------------------------
+    const int cons = warp - kGtProd;
+    const int cw_id = cons % kGtGroups;             // weight rows 16 cw_id .. + 15
+    const int kpart = cons / kGtGroups;             // KSPLIT == 2: chunk kpart of each unit
+    const int g = lane >> 2, j = lane & 3;
+    const int row0 = 16 * cw_id + g, row1 = row0 + 8;
+    const uint32_t sw = (uint32_t)(g & 7);         // row0 % 8 == row1 % 8 == g
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // xs written by the X-preparation grid
+
+    float acc[1][NT][4];
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[0][t][e] = 0.0f;
+
+    const int first_tile = (int)(it0 / KS);
+    auto slot_of = [&](int cta, int tile) -> int {
+      return 2 * cta + ((int)(((long long)cta * a.T / a.G) / KS) == tile ? 0 : 1);
+    };
+    auto store = [&](int tile, float (&v)[1][NT][4]) {
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int n = tile * kGtRows + 16 * cw_id + g + ((e & 2) ? 8 : 0);
+          const int m = 8 * t + 2 * j + (e & 1);
+          if (n < a.N && m < a.M) {
+            float y = v[0][t][e] * __ldg(a.xs + m);
+            if (FMT == 1) y *= a.ts;
+            if (F32OUT) static_cast<float*>(a.Y)[(size_t)m * a.ldy + n] = y;
+            else static_cast<__nv_bfloat16*>(a.Y)[(size_t)m * a.ldy + n] = __float2bfloat16_rn(y);
+          }
+        }
+      }
+    };
+    auto flush = [&](int tile, bool whole) {
+      if (C::KSPLIT == 2) {  // chunk-1 warps hand their sums to the chunk-0 warps (fixed order)
+        if (kpart == 1) {
+#pragma unroll
+          for (int t = 0; t < NT; ++t)
+            s_half[(cw_id * NT + t) * 32 + lane] = make_float4(acc[0][t][0], acc[0][t][1], acc[0][t][2], acc[0][t][3]);
+        }
+        asm volatile("bar.sync 2, %0;" ::"r"(kGtCons * 32) : "memory");
+        if (kpart == 0) {
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+            const float4 h = s_half[(cw_id * NT + t) * 32 + lane];
+            acc[0][t][0] += h.x; acc[0][t][1] += h.y; acc[0][t][2] += h.z; acc[0][t][3] += h.w;
+          }
+        }
+        asm volatile("bar.sync 2, %0;" ::"r"(kGtCons * 32) : "memory");  // s_half is reused
+        if (kpart == 1) {
+#pragma unroll
+          for (int t = 0; t < NT; ++t)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[0][t][e] = 0.0f;
+          return;
+        }
+      }
+      if (whole) {
+        store(tile, acc);
+      } else {
+        float4* mine = reinterpret_cast<float4*>(a.partials) +
+                       ((size_t)slot_of((int)blockIdx.x, tile) * kGtGroups + cw_id) * NT * 32;
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+          __stcg(mine + t * 32 + lane, make_float4(acc[0][t][0], acc[0][t][1], acc[0][t][2], acc[0][t][3]));
+        __threadfence();
+        asm volatile("bar.sync 1, %0;" ::"r"(kGtGroups * 32) : "memory");
+        if (cw_id == 0 && lane == 0) *s_ticket = ok ? atomicAdd(a.counters + tile, 1u) : 0xFFFFFFFFu;
+        asm volatile("bar.sync 1, %0;" ::"r"(kGtGroups * 32) : "memory");
+        const unsigned ticket = *s_ticket;
+        const long long t0 = (long long)tile * KS, t1 = t0 + KS - 1;
+        const int c_lo = (int)(((t0 + 1) * a.G - 1) / a.T), c_hi = (int)(((t1 + 1) * a.G - 1) / a.T);
+        if (ticket == (unsigned)(c_hi - c_lo)) {  // last contributor: sum in CTA order
+          __threadfence();
+          float sum[1][NT][4];
+#pragma unroll
+          for (int t = 0; t < NT; ++t)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) sum[0][t][e] = 0.0f;
+          for (int cc = c_lo; cc <= c_hi; ++cc) {
+            const float4* src = reinterpret_cast<const float4*>(a.partials) +
+                                ((size_t)slot_of(cc, tile) * kGtGroups + cw_id) * NT * 32;
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+              const float4 pv = __ldcg(src + t * 32 + lane);
+              sum[0][t][0] += pv.x; sum[0][t][1] += pv.y; sum[0][t][2] += pv.z; sum[0][t][3] += pv.w;
+            }
+          }
+          store(tile, sum);
+          if (cw_id == 0 && lane == 0) a.counters[tile] = 0u;  // leave the workspace zeroed
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(kGtGroups * 32) : "memory");  // s_ticket is reused
+      }
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[0][t][e] = 0.0f;
+    };
+    (void)first_tile;
+
+    int tile = (int)(it0 / KS), ks = (int)(it0 % KS);
+    bool seg_whole = (ks == 0);
+    for (int i = 0; i < niter; ++i) {
+      const int s = i % S;
+      if (ok) ok = mbar_wait_flag(full_bar(s), (i / S) & 1, fault);
+      ok = __all_sync(0xFFFFFFFFu, ok);
+      if (ok) {
+        const uint8_t* W = gbase + W_off(s);
+        const uint8_t* X = gbase + X_off(s);
+        const uint8_t* SC = gbase + S_off(s);
+#pragma unroll
+        for (int cc2 = 0; cc2 < 2 / C::KSPLIT; ++cc2) {
+          const int c = (C::KSPLIT == 2) ? kpart : cc2;
+          uint32_t cw[1][2][4], cs[1][2], cx[NT][16];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int row = h ? row1 : row0;
+            const uint8_t* wr = W + row * 128;
+            if (FMT == 0) {  // 4 bytes of each of the chunk's 4 blocks
+#pragma unroll
+              for (int b = 0; b < 4; ++b)
+                cw[0][h][b] = *reinterpret_cast<const uint32_t*>(wr + ((((uint32_t)(4 * c + b)) ^ sw) << 4) + 4 * j);
+              cs[0][h] = *reinterpret_cast<const uint32_t*>(SC + row * C::SB + 4 * c);
+            } else {         // 16 contiguous bytes
+              const uint4 v = *reinterpret_cast<const uint4*>(wr + ((((uint32_t)(4 * c + j)) ^ sw) << 4));
+              cw[0][h][0] = v.x; cw[0][h][1] = v.y; cw[0][h][2] = v.z; cw[0][h][3] = v.w;
+              cs[0][h] = *reinterpret_cast<const uint16_t*>(SC + row * C::SB + 8 * c + 2 * j);
+            }
+          }
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+            const int m = 8 * t + g;
+            const uint8_t* xr = X + m * (kGtUnitK * 2);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int idx = (FMT == 0) ? 16 * c + 4 * q + j : 16 * c + 4 * j + q;  // 8-f16 chunk of the unit
+              const int pos = (idx & ~7) | ((idx ^ m) & 7);
+              const uint4 v = *reinterpret_cast<const uint4*>(xr + pos * 16);
+              cx[t][4 * q] = v.x; cx[t][4 * q + 1] = v.y; cx[t][4 * q + 2] = v.z; cx[t][4 * q + 3] = v.w;
+            }
+          }
+          chunk_mma<FMT, 1, NT>(acc, cw, cs, cx);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty_bar(s));  // this warp is done with the stage
+      if (ks == KS - 1 || i == niter - 1) {
+        flush(tile, seg_whole && ks == KS - 1);
+        seg_whole = true;
+      }
+      if (++ks == KS) { ks = 0; ++tile; }
+    }
+  }
+
+  if (!ok) {
+    atomicExch(fault, 1u);
+    if (threadIdx.x == 0) {  // give copies in flight a bounded chance to land
+      const unsigned long long t0 = gtimer();
+      while (gtimer() - t0 < 50000000ull) { }
+    }
+  }
+  __syncthreads();
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+bool make_tma_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr, uint64_t inner, uint64_t outer,
+                     uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw);
+
+bool gemv_tma_supported(const qgemm_weights_t* w, int mb) {
+  return mb >= 1 && mb <= 16 && (w->format == QGEMM_FMT_MXFP4 || w->format == QGEMM_FMT_NVFP4) &&
+         w->K % kGtUnitK == 0 && w->K <= (size_t)INT32_MAX / 2 && w->N <= (size_t)INT32_MAX / 2 &&
+         (reinterpret_cast<uintptr_t>(w->scales) & 3u) == 0;
+}
+
+struct GtPlan {
+  int nt, mpad, tiles, KS, G;
+  long long T;
+  size_t counter_bytes, partial_bytes, xg_bytes;
+};
+static GtPlan gt_plan(const qgemm_weights_t* w, int mb, int sm_count) {
+  GtPlan p;
+  p.nt = mb <= 8 ? 1 : 2;
+  p.mpad = 8 * p.nt;
+  p.tiles = (int)((w->N + kGtRows - 1) / kGtRows);
+  p.KS = (int)(w->K / kGtUnitK);
+  p.T = (long long)p.tiles * p.KS;
+  p.G = (int)(p.T < sm_count ? p.T : sm_count);
+  p.counter_bytes = ((size_t)p.tiles * sizeof(unsigned) + 255) & ~(size_t)255;
+  p.partial_bytes = (((size_t)2 * p.G * kGtGroups * p.nt * 32 * sizeof(float4)) + 255) & ~(size_t)255;
+  p.xg_bytes = (((size_t)16 * w->K * 2) + 255) & ~(size_t)255;  // room for mpad = 16
+  return p;
+}
+// [counters | partials | X image (16 rows)]; xs lives with the caller's layout
+size_t gemv_tma_workspace(const qgemm_weights_t* w, int sm_count) {
+  const GtPlan p = gt_plan(w, 16, sm_count);
+  return p.counter_bytes + p.partial_bytes + p.xg_bytes;
+}
+
+template <int FMT, int NT, bool F32>
+static cudaError_t launch_gt_t(const CUtensorMap& mw, const GtArgs& a, cudaStream_t s) {
+  constexpr int BYTES = GtCfg<FMT, NT>::BYTES;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr[dev]) {
+    e = cudaFuncSetAttribute(k_gemv_tma<FMT, NT, F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, BYTES);
+    if (e != cudaSuccess) return e;
+    attr[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)a.G);
+  cfg.blockDim = dim3(GtCfg<FMT, NT>::THREADS);
+  cfg.dynamicSmemBytes = BYTES;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_gemv_tma<FMT, NT, F32>, mw, a);
+}
+
+// One launch over mb <= 16 activation rows whose X image (layout 2 of
+// k_xprep, mpad = 8 * ceil(mb / 8)) and row factors are already in xg / xs.
+// ws: gemv_tma_workspace bytes, counters zero.
+qgemm_status_t gemm_gemv_tma(const qgemm_weights_t* w, const __half* xg, const float* xs, int mb, void* Y, int ldy,
+                             bool f32, void* ws, int sm_count, cudaStream_t s) {
+  if (!gemv_tma_supported(w, mb)) return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "TMA decode path: unsupported shape");
+  if (sm_count <= 0) return fail(QGEMM_ERR_CUDA, "TMA decode path: no device properties");
+  const GtPlan p = gt_plan(w, mb, sm_count);
+  CUtensorMap mw;
+  if (!make_tma_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->data, w->K / 2, w->N, w->K / 2, kGtUnitK / 2, kGtRows,
+                       CU_TENSOR_MAP_SWIZZLE_128B))
+    return fail(QGEMM_ERR_CUDA, "TMA decode path: cuTensorMapEncodeTiled failed");
+  GtArgs a;
+  a.scales = static_cast<const uint8_t*>(w->scales);
+  a.xg = reinterpret_cast<const uint8_t*>(xg);
+  a.xs = xs;
+  a.Y = Y;
+  a.counters = static_cast<unsigned*>(ws);
+  a.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + p.counter_bytes);
+  a.T = p.T; a.M = mb; a.N = (int)w->N; a.K = (int)w->K; a.ldy = ldy;
+  a.KS = p.KS; a.G = p.G; a.ts = w->tensor_scale;
+  cudaError_t e;
+  if (w->format == QGEMM_FMT_MXFP4) {
+    if (p.nt == 1) e = f32 ? launch_gt_t<0, 1, true>(mw, a, s) : launch_gt_t<0, 1, false>(mw, a, s);
+    else e = f32 ? launch_gt_t<0, 2, true>(mw, a, s) : launch_gt_t<0, 2, false>(mw, a, s);
+  } else {
+    if (p.nt == 1) e = f32 ? launch_gt_t<1, 1, true>(mw, a, s) : launch_gt_t<1, 1, false>(mw, a, s);
+    else e = f32 ? launch_gt_t<1, 2, true>(mw, a, s) : launch_gt_t<1, 2, false>(mw, a, s);
+  }
+  if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "TMA decode launch: %s", cudaGetErrorString(e));
+  return QGEMM_OK;
+}
+
+size_t gemv_tma_xg_offset(const qgemm_weights_t* w, int sm_count) {
+  const GtPlan p = gt_plan(w, 16, sm_count);
+  return p.counter_bytes + p.partial_bytes;
+}
+
+unsigned gemv_tma_fault() {
+  unsigned f = 0;
+  if (cudaMemcpyFromSymbol(&f, g_gemv_tma_fault, sizeof(f)) != cudaSuccess) return 0xFFFFFFFFu;
+  return f;
+}
+
+}  // namespace qg

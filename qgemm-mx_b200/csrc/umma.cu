@@ -722,6 +722,7 @@ qgemm_status_t gemm_umma_ts(const qgemm_weights_t* w, const __half* Xh, const fl
 }
 
 unsigned umma_sk_fault();
+unsigned gemv_tma_fault();
 
 }  // namespace qg
 
@@ -732,9 +733,9 @@ extern "C" {
 qgemm_status_t qgemm_umma_status(int32_t* faulted) {
   unsigned f = 0;
   QG_CUDA_RET(cudaMemcpyFromSymbol(&f, g_umma_fault, sizeof(f)));
-  const unsigned g = umma_sk_fault();
-  if (g == 0xFFFFFFFFu) return fail(QGEMM_ERR_CUDA, "umma: reading the stream-K fault flag failed");
-  f |= g;
+  const unsigned g = umma_sk_fault(), h = gemv_tma_fault();
+  if (g == 0xFFFFFFFFu || h == 0xFFFFFFFFu) return fail(QGEMM_ERR_CUDA, "umma: reading a fault flag failed");
+  f |= g | h;
   if (faulted) *faulted = (int32_t)f;
   return f ? fail(QGEMM_ERR_TIMEOUT, "umma: a bounded barrier wait gave up") : QGEMM_OK;
 }
