@@ -228,8 +228,12 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
     }
   } else if (warp == kSkMmaWarp) {
     // ------------------------------ MMA issuer --------------------------------
-    if (lane == 0) {
+    // The whole warp runs the loop, so the operand arithmetic stays warp-
+    // uniform; one elected lane issues the MMAs and commits.
+    {
       constexpr uint32_t idesc = idesc_f16(kSkRows, BN);
+      uint32_t leader;
+      asm volatile("{ .reg .pred p; elect.sync _|p, 0xFFFFFFFF; selp.u32 %0, 1, 0, p; }" : "=r"(leader));
       int kt = (int)(it0 % KS), seg = 0;
       for (int i = 0; i < niter; ++i) {
         const int sx = i % SX, sa = i % AST;
@@ -240,17 +244,35 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
         if (first && seg >= 2) ok = mbar_wait_flag(acce_bar(b), ((seg >> 1) + 1) & 1, fault);
         ok = ok && mbar_wait_flag(aready_bar(sa), (i / AST) & 1, fault) &&
              mbar_wait_flag(fullx_bar(sx), (i / SX) & 1, fault);
+        ok = __all_sync(0xFFFFFFFFu, ok);
         if (!ok) break;
         tc_fence_after();
         const uint64_t d0 = sw128_desc(X_addr(sx));
         const uint32_t ta = tmem_a + (uint32_t)(sa * 128), td = tmem + (uint32_t)(b * BN);
+        const uint32_t acc0 = first ? 0u : 1u;
 #pragma unroll
-        for (int kk = 0; kk < kSkBK / 16; ++kk)  // A: 8 TMEM columns per K=16; B: sub-tile kk/4, +32 bytes per K=16
-          umma_f16_ts(td, ta + (uint32_t)(kk * 8), d0 + (uint64_t)((kk >> 2) * (C::XBOX >> 4) + 2 * (kk & 3)),
-                      idesc, (!first || kk > 0) ? 1u : 0u);
-        umma_commit(emptyx_bar(sx));
-        umma_commit(afree_bar(sa));
-        if (last) umma_commit(accf_bar(b));
+        for (int g4 = 0; g4 < kSkBK / 64; ++g4) {  // sub-tile g4 of X: 4 MMAs of K = 16
+          const uint64_t dg = d0 + (uint64_t)(g4 * (C::XBOX >> 4));
+          const uint32_t ag = ta + (uint32_t)(g4 * 32);
+          asm volatile(
+              "{ .reg .pred L, A, T;\n"
+              "  setp.ne.b32 L, %0, 0;\n"
+              "  setp.ne.b32 A, %1, 0;\n"
+              "  setp.eq.b32 T, %0, %0;\n"
+              "  @L tcgen05.mma.cta_group::1.kind::f16 [%2], [%3], %4, %5, A;\n"
+              "  @L tcgen05.mma.cta_group::1.kind::f16 [%2], [%6], %7, %5, T;\n"
+              "  @L tcgen05.mma.cta_group::1.kind::f16 [%2], [%8], %9, %5, T;\n"
+              "  @L tcgen05.mma.cta_group::1.kind::f16 [%2], [%10], %11, %5, T; }\n"
+              ::"r"(leader), "r"(g4 == 0 ? acc0 : 1u), "r"(td), "r"(ag), "l"(dg), "r"(idesc),
+                "r"(ag + 8u), "l"(dg + 2), "r"(ag + 16u), "l"(dg + 4), "r"(ag + 24u), "l"(dg + 6)
+              : "memory");
+        }
+        if (leader) {
+          umma_commit(emptyx_bar(sx));
+          umma_commit(afree_bar(sa));
+          if (last) umma_commit(accf_bar(b));
+        }
+        __syncwarp();
         if (++kt == KS) kt = 0;
       }
     }
