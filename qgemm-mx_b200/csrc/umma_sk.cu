@@ -76,11 +76,12 @@ constexpr int kSkDqWarps = 16;
 constexpr int kSkEpiWarps = 4;
 constexpr int kSkEpiWarp0 = kSkDqWarp0 + kSkDqWarps;
 constexpr int kSkThreads = 32 * (kSkEpiWarp0 + kSkEpiWarps);  // 768
-constexpr int kSkScaleAhead = 8;                         // scale prefetch distance (steps)
 
 template <int BN>
 struct SkCfg {
-  static constexpr int W_STAGE = kSkRows * kSkBK / 2;    // 16 KB packed codes
+  static constexpr int W_CODES = kSkRows * kSkBK / 2;    // 16 KB packed codes
+  static constexpr int W_SCALE_ROW = 16;                 // scale bytes per row per step (MXFP4 8, NVFP4 16)
+  static constexpr int W_STAGE = W_CODES + kSkRows * W_SCALE_ROW;
   static constexpr int XBOX = BN * 128;                  // 64 k of X (f16), one swizzle row per activation row
   static constexpr int X_STAGE = 4 * XBOX;
   static constexpr int SX = BN == 32 ? 4 : 3;            // X ring depth
@@ -172,7 +173,10 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < SX; ++s) { mbar_init(fullx_bar(s), 1); mbar_init(emptyx_bar(s), 1); }
-    for (int s = 0; s < SW; ++s) { mbar_init(fullw_bar(s), 1); mbar_init(emptyw_bar(s), kSkDqWarps); }
+    for (int s = 0; s < SW; ++s) {  // full: expect_tx arrival + 32 cp.async arrivals (scale bytes)
+      mbar_init(fullw_bar(s), 1 + 32);
+      mbar_init(emptyw_bar(s), kSkDqWarps);
+    }
     for (int s = 0; s < AST; ++s) { mbar_init(aready_bar(s), kSkDqWarps); mbar_init(afree_bar(s), 1); }
     for (int b = 0; b < 2; ++b) {
       mbar_init(accf_bar(b), 1);
@@ -214,16 +218,37 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
     }
   } else if (warp < kSkWProd0 + kSkWProds) {
     // ------------------------------ W producers -------------------------------
-    if (lane == 0) {
+    // Lane 0 arms the stage and issues the packed-W box; all 32 lanes copy the
+    // step's scale bytes (4-byte cp.async) next to it and arrive on the same
+    // mbarrier when their copies land.
+    {
       const int p = warp - kSkWProd0;
+      constexpr int SBY = (FMT == 0) ? kSkBK / 32 : kSkBK / 16;  // scale bytes per row per step
+      constexpr int WPR = SBY / 4;
+      const size_t srow = (size_t)a.K / (FMT == 0 ? 32 : 16);
+      int tile = (int)((it0 + p) / KS), ks = (int)((it0 + p) % KS);
       for (int i = p; i < niter; i += kSkWProds) {
         const int s = i % SW;
-        if (i >= SW) ok = mbar_wait_flag(emptyw_bar(s), ((i / SW) + 1) & 1, fault);
+        if (i >= SW && lane == 0) ok = mbar_wait_flag(emptyw_bar(s), ((i / SW) + 1) & 1, fault);
+        ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
         if (!ok) break;
-        const long long it = it0 + i;
-        const int tile = (int)(it / KS), ks = (int)(it % KS);
-        mbar_expect_tx(fullw_bar(s), (uint32_t)C::W_STAGE);
-        tma_load_2d(base + (uint32_t)W_off(s), &map_w, ks * (kSkBK / 2), (tile % a.tiles_n) * kSkRows, fullw_bar(s));
+        const int n0 = (tile % a.tiles_n) * kSkRows;
+        if (lane == 0) {
+          mbar_expect_tx(fullw_bar(s), (uint32_t)C::W_CODES);
+          tma_load_2d(base + (uint32_t)W_off(s), &map_w, ks * (kSkBK / 2), n0, fullw_bar(s));
+        }
+#pragma unroll
+        for (int e = lane; e < kSkRows * WPR; e += 32) {
+          const int row = e / WPR, wi = e % WPR;
+          const int n = (n0 + row < a.N) ? n0 + row : a.N - 1;  // rows past N: their codes are zero-filled
+          const uint8_t* src = a.scales + (size_t)n * srow + (size_t)ks * SBY + 4 * wi;
+          asm volatile("cp.async.ca.shared.global [%0], [%1], 4;"
+                       ::"r"(base + (uint32_t)(W_off(s) + C::W_CODES + row * C::W_SCALE_ROW + 4 * wi)), "l"(src)
+                       : "memory");
+        }
+        asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(fullw_bar(s)) : "memory");
+        ks += kSkWProds;
+        while (ks >= KS) { ks -= KS; ++tile; }
       }
     }
   } else if (warp == kSkMmaWarp) {
@@ -285,35 +310,22 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
     // SWIZZLE_128B: 16-byte chunk c of 128-byte row r sits at chunk c ^ (r % 8)
     const uint32_t w_c0 = (uint32_t)(r * 128 + (((2 * j) ^ (r & 7)) << 4));
     const uint32_t w_c1 = (uint32_t)(r * 128 + (((2 * j + 1) ^ (r & 7)) << 4));
-    // Scale bits of this thread's 64 k (MXFP4 two E8M0 bytes, NVFP4 four E4M3
-    // bytes), loaded kSkScaleAhead steps ahead into a register ring.  Every
-    // load reads a valid address (rows past N and steps past the range are
-    // clamped: TMA zero-fills those rows' codes, so their factors never reach
-    // a stored output), so no select waits on a load in flight.
-    const size_t srow = (FMT == 0) ? (size_t)a.K / 32 : (size_t)a.K / 16;
-    const uint8_t* sc_col = a.scales + (FMT == 0 ? 2 * j : 4 * j);
-    int p_tile = (int)(it0 / KS), p_k = (int)(it0 % KS);
-    const uint8_t* p_row = nullptr;
-    auto row_ptr = [&](int t) {
-      int n = (t % a.tiles_n) * kSkRows + r;
-      n = n < a.N ? n : a.N - 1;
-      return sc_col + (size_t)n * srow;
+    // this thread's scale bits in a W stage: MXFP4 two E8M0 bytes, NVFP4 four E4M3 bytes
+    const uint32_t sc_off = (uint32_t)(C::W_CODES + r * C::W_SCALE_ROW + (FMT == 0 ? 2 * j : 4 * j));
+    auto load_step = [&](int i, uint4& c0, uint4& c1, uint32_t& sc) -> bool {
+      const int sw = i % SW;
+      bool okw = mbar_wait_flag(fullw_bar(sw), (i / SW) & 1, fault);
+      okw = __all_sync(0xFFFFFFFFu, okw);
+      if (!okw) return false;
+      const uint8_t* st = gbase + W_off(sw);
+      c0 = *reinterpret_cast<const uint4*>(st + w_c0);
+      c1 = *reinterpret_cast<const uint4*>(st + w_c1);
+      sc = (FMT == 0) ? (uint32_t)*reinterpret_cast<const uint16_t*>(st + sc_off)
+                      : *reinterpret_cast<const uint32_t*>(st + sc_off);
+      return true;
     };
-    p_row = row_ptr(p_tile);
-    auto next_scale = [&]() -> uint32_t {  // scale bits of step (p_tile, p_k), then advance (clamped at the end)
-      const uint32_t v = (FMT == 0) ? (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(p_row + p_k * 8))
-                                    : __ldg(reinterpret_cast<const uint32_t*>(p_row + p_k * 16));
-      const long long cur = (long long)p_tile * KS + p_k;
-      if (cur + 1 < it1) {
-        if (++p_k == KS) { p_k = 0; ++p_tile; p_row = row_ptr(p_tile); }
-      }
-      return v;
-    };
-    uint32_t ring[kSkScaleAhead];
-#pragma unroll
-    for (int u = 0; u < kSkScaleAhead; ++u) ring[u] = next_scale();
     // 32 codes -> 16 f16x2 words with their block factors applied
-    auto widen = [&](uint4 pk4, uint32_t f_lo, uint32_t f_hi, uint32_t (&o)[16]) {
+    auto widen = [&](uint4 pk4, uint32_t f_lo, uint32_t f_hi, uint32_t* o) {
       e2m1x8_to_f16x2(pk4.x, o);
       e2m1x8_to_f16x2(pk4.y, o + 4);
       e2m1x8_to_f16x2(pk4.z, o + 8);
@@ -321,8 +333,13 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
 #pragma unroll
       for (int u = 0; u < 16; ++u) o[u] = hmul2_f16x2(o[u], u < 8 ? f_lo : f_hi);
     };
+    // Software pipeline: step i's codes and scales were loaded during step
+    // i - 1; step i + 1's are loaded while step i's TMEM store is in flight.
     int kt = (int)(it0 % KS), seg = 0, rb = 0;
-    for (int i = 0; i < niter; ++i) {
+    uint4 c0 = make_uint4(0, 0, 0, 0), c1 = c0;
+    uint32_t sc = 0;
+    if (niter > 0) ok = load_step(0, c0, c1, sc);
+    for (int i = 0; i < niter && ok; ++i) {
       const bool first = (i == 0) || (kt == 0);
       if (first && i > 0) ++seg;
       if (FMT == 0 && first) {
@@ -335,10 +352,6 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
         if (lane == 0) mbar_arrive(basee_bar(b));
       }
       const int sw = i % SW, sa = i % AST;
-      const uint32_t sc = ring[0];
-#pragma unroll
-      for (int u = 0; u + 1 < kSkScaleAhead; ++u) ring[u] = ring[u + 1];
-      ring[kSkScaleAhead - 1] = next_scale();
       uint32_t f0, f1, f2, f3;  // factors of the four 16-code halves of the two chunks
       if (FMT == 0) {
         const uint32_t b0 = sc & 0xFFu, b1 = (sc >> 8) & 0xFFu;
@@ -348,22 +361,16 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
         f0 = f16x2_e4m3(sc & 0xFFu); f1 = f16x2_e4m3((sc >> 8) & 0xFFu);
         f2 = f16x2_e4m3((sc >> 16) & 0xFFu); f3 = f16x2_e4m3(sc >> 24);
       }
-
-      ok = mbar_wait_flag(fullw_bar(sw), (i / SW) & 1, fault);
-      ok = __all_sync(0xFFFFFFFFu, ok);
-      if (!ok) break;
-      const uint4 c0 = *reinterpret_cast<const uint4*>(gbase + W_off(sw) + w_c0);
-      const uint4 c1 = *reinterpret_cast<const uint4*>(gbase + W_off(sw) + w_c1);
-      uint32_t o0[16], o1[16];
-      widen(c0, f0, f1, o0);
-      widen(c1, f2, f3, o1);
+      uint32_t o[32];
+      widen(c0, f0, f1, o);
+      widen(c1, f2, f3, o + 16);
       __syncwarp();                                   // every lane's codes are in registers:
       if (lane == 0) mbar_arrive(emptyw_bar(sw));     // the W stage may be refilled
       if (i >= AST) ok = mbar_wait_flag(afree_bar(sa), ((i / AST) + 1) & 1, fault);
       ok = __all_sync(0xFFFFFFFFu, ok);
       if (!ok) break;
-      tmem_st16(tmem_a + t_lane + (uint32_t)(sa * 128 + 32 * j), o0);
-      tmem_st16(tmem_a + t_lane + (uint32_t)(sa * 128 + 32 * j + 16), o1);
+      tmem_st32(tmem_a + t_lane + (uint32_t)(sa * 128 + 32 * j), o);
+      if (i + 1 < niter) ok = load_step(i + 1, c0, c1, sc);  // overlaps the store
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
       __syncwarp();
