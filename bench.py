@@ -14,10 +14,15 @@ rows of every W (and its scales), computes its Y slice and an NCCL all-gather
           time (formats.cuh:80-83 accounting), device-resident inputs, each
           step one CUDA-graph replay (the reference's time_graphed protocol).
   e2e     the same bytes / time of the same step through the C-ABI with host
-          buffers: pinned X copied in and Y copied out for every call.
-  roofline  the decode kernel's per-launch algorithmic bytes / its mean launch
-          time, measured per (layer, M) with CUDA events over graph replays
-          of weight-rotated launches (L2-cold), against the measured HBM peak.
+          buffers: every step copies its distinct activations in from pinned
+          host memory and reads every Y back to pinned host memory.
+  roofline  for the GEMM kernel with the largest share of the step
+          (qgemm_launch_count names it per call): its algorithmic bytes per
+          launch / its mean launch time, measured per (layer, M) with CUDA
+          events over graph replays of weight-rotated launches (L2-cold),
+          against the measured HBM peak; "kernels" lists every GEMM kernel's
+          figures; traffic is the ncu DRAM bytes per launch recorded in
+          profiles/dram_traffic.json for the same shapes.
 
 --impl reference times the reference's own CPU path (dequant_* +
 gemm_fp32_ref, threaded over rows; oracle/_ref, else the oracle port) on a
@@ -373,7 +378,8 @@ def main():
     torch.cuda.synchronize()
 
     calls = [(M, name, N, K) for M in ms for name, N, K in layers]
-    launches_per_step = sum(math.ceil(M / 32) for M, *_ in calls)
+    kernel_of = {(M, name): qg.launch_count(shards[name], M)[1] for M, name, N, K in calls}
+    launches_per_step = sum(qg.launch_count(shards[name], M)[0] for M, name, N, K in calls)
     bytes_rank = sum(qg.total_bytes(fcode, M, N // world, K) for M, name, N, K in calls)
     bytes_step = bytes_rank * world
 
@@ -429,18 +435,29 @@ def main():
     clk = clocks.summary()
 
     # ---- e2e: same step through the C-ABI with host buffers ----------------
+    # Every step copies its distinct activations host -> device (pinned), runs
+    # the 12 GEMMs and reads every Y back to pinned host memory; the read-backs
+    # run on a copy stream behind each GEMM, overlapping the later GEMMs.
     Xh = {k: torch.empty(v.shape, dtype=v.dtype, pin_memory=True).copy_(v.cpu()) for k, v in X.items()}
     Yh = {k: torch.empty(v.shape, dtype=v.dtype, pin_memory=True) for k, v in (Yfull or Y).items()}
     Xd = {(M, K): torch.empty_like(X[(M, K)]) for (M, K) in X}
-    h2d = sum(M * K * 2 for M, name, N, K in calls)
+    h2d = sum(v.numel() * 2 for v in Xh.values())
     d2h = sum(M * N * 2 for M, name, N, K in calls)
+    cs = torch.cuda.Stream(device=dev)
+    done = {(M, name): torch.cuda.Event() for M, name, N, K in calls}
 
     def e2e_step():
+        main = torch.cuda.current_stream()
+        for key in Xd:
+            Xd[key].copy_(Xh[key], non_blocking=True)
         for M, name, N, K in calls:
-            Xd[(M, K)].copy_(Xh[(M, K)], non_blocking=True)
             qg.gemm_w4a16(shards[name], Xd[(M, K)], out=Y[(M, name)], workspace=ws[(M, name)])
             gather(M, name)
-            Yh[(M, name)].copy_((Yfull or Y)[(M, name)], non_blocking=True)
+            done[(M, name)].record(main)
+            cs.wait_event(done[(M, name)])
+            with torch.cuda.stream(cs):
+                Yh[(M, name)].copy_((Yfull or Y)[(M, name)], non_blocking=True)
+        main.wait_stream(cs)  # the step ends when every result is on the host
 
     for _ in range(max(3, args.warmup)):
         e2e_step()
@@ -491,16 +508,29 @@ def main():
         nb = qg.total_bytes(fcode, M, p.N, K)
         ktime += us * 1e-6
         kbytes += nb
-        table.append((name, M, p.N, K, rot, us, nb / (us * 1e-6) / 1e9))
+        table.append((name, M, p.N, K, rot, us, nb / (us * 1e-6) / 1e9, kernel_of[(M, name)]))
         del copies, g2
         torch.cuda.empty_cache()
     peak, peak_src = measured_peaks()
-    achieved = kbytes / ktime / 1e9
+    # per GEMM kernel: algorithmic bytes per launch / mean launch time; the
+    # roofline entry is the kernel with the largest share of the step
+    per_kernel = {}
+    for name, M, N, K, rot, us, gbs, kern in table:
+        d = per_kernel.setdefault(kern, {"us": 0.0, "bytes": 0, "launches": 0, "shapes": []})
+        d["us"] += us
+        d["bytes"] += qg.total_bytes(fcode, M, N, K)
+        d["launches"] += 1
+        d["shapes"].append(f"{name}:M={M}")
+    dom = max(per_kernel, key=lambda k: per_kernel[k]["us"])
+    achieved = per_kernel[dom]["bytes"] / (per_kernel[dom]["us"] * 1e-6) / 1e9
     traffic = None
-    tr_path = os.path.join(ROOT, "profiles", "gemv_traffic.json")
-    if os.path.exists(tr_path):
+    tr_path = os.path.join(ROOT, "profiles", "dram_traffic.json")
+    if os.path.exists(tr_path) and world == 1:
         with open(tr_path) as f:
-            traffic = json.load(f).get("bytes_per_launch")
+            trd = json.load(f).get(args.workload, {}).get(dom, {})
+        got = [trd[sh] for sh in per_kernel[dom]["shapes"] if sh in trd]
+        if got and len(got) == len(per_kernel[dom]["shapes"]):
+            traffic = round(sum(got) / len(got))  # DRAM bytes per launch, ncu capture
 
     # ---- CPU baseline (rank 0 at N=1 only) ---------------------------------
     cpu = None
@@ -508,15 +538,19 @@ def main():
         O, impl, kind = cpu_path()
         threads = os.cpu_count() or 1
         rows = calibrate_rows(fmt, layers, ms, threads, O, impl, 12.0)
-        secs, nb = cpu_sample_run(fmt, layers, ms, rows, threads, O, impl, {})
+        cache = {}
+        secs, nb, reps = 0.0, 0, 0
+        while secs < 12.0 and reps < 64:  # repeat the bounded sample to ~12 s of CPU work
+            s1, b1 = cpu_sample_run(fmt, layers, ms, rows, threads, O, impl, cache)
+            secs, nb, reps = secs + s1, nb + b1, reps + 1
         cpu = {"value": round(nb / secs / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": kind,
                "sample": f"{rows} rows of each layer x M in {ms} (dequant + gemm_fp32_ref), "
-                         f"{secs:.1f} s"}
+                         f"{reps} passes, {secs:.1f} s"}
 
     if args.table and rank == 0:
-        print(f"{'layer':8s} {'M':>4s} {'N':>6s} {'K':>6s} {'rot':>3s} {'us':>9s} {'GB/s':>8s}", file=sys.stderr)
-        for name, M, N, K, rot, us, gbs in table:
-            print(f"{name:8s} {M:4d} {N:6d} {K:6d} {rot:3d} {us:9.2f} {gbs:8.1f}", file=sys.stderr)
+        print(f"{'layer':8s} {'M':>4s} {'N':>6s} {'K':>6s} {'rot':>3s} {'us':>9s} {'GB/s':>8s}  kernel", file=sys.stderr)
+        for name, M, N, K, rot, us, gbs, kern in table:
+            print(f"{name:8s} {M:4d} {N:6d} {K:6d} {rot:3d} {us:9.2f} {gbs:8.1f}  {kern}", file=sys.stderr)
 
     if rank == 0:
         line = {
@@ -534,8 +568,14 @@ def main():
                     "d2h_bytes_per_step": d2h * world},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "kernel": dom, "share": round(per_kernel[dom]["us"] / sum(v["us"] for v in per_kernel.values()), 3),
+                         "algorithmic_bytes_per_launch": round(per_kernel[dom]["bytes"] / per_kernel[dom]["launches"]),
                          "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured"
-                         else "fallback 6650 GB/s"},
+                         else "fallback 6650 GB/s",
+                         "kernels": {k: {"achieved": round(v["bytes"] / (v["us"] * 1e-6) / 1e9, 1),
+                                         "frac": round(v["bytes"] / (v["us"] * 1e-6) / 1e9 / peak, 4),
+                                         "us_per_step": round(v["us"], 2), "launches_per_step": v["launches"]}
+                                     for k, v in per_kernel.items()}},
             "cpu_baseline": cpu,
             "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"],
                        "samples": clk["samples"]},

@@ -119,6 +119,12 @@ qgemm_status_t qgemm_codec_encode(int32_t kind, const float* in, void* out,
  * again.  Calls that may overlap on the GPU need distinct workspaces.        */
 size_t qgemm_workspace_size(const qgemm_weights_t* w, int32_t M);
 qgemm_status_t qgemm_workspace_init(void* workspace, size_t ws_bytes, void* stream);
+/* Number of kernel launches one qgemm_gemm_w4a16 call makes for (w, M), and
+ * which GEMM kernel it uses (0 LDG-fed decode, 1 TMA-fed decode, 2 stream-K
+ * tcgen05, 3 tile-per-CTA tcgen05).  Returns -1 for invalid arguments.  No
+ * counterpart in the reference (its benches launch one kernel per GEMM);
+ * used for launch accounting in benchmarks. */
+int32_t qgemm_launch_count(const qgemm_weights_t* w, int32_t M, int32_t* kernel);
 
 /* Y = X . W^T.  X: bf16 bits [M,K]; Y: bf16 bits [M,N].  Any M >= 1.
  * Result is within the reference GEMM (ref_gemm.hpp:15-27, double

@@ -68,6 +68,7 @@ _sig("qgemm_nvfp4_tensor_scale", _i32, [_vp, _sz, _vp, _vp])
 _sig("qgemm_dequant", _i32, [C.POINTER(_Weights), _vp, _vp])
 _sig("qgemm_codec_encode", _i32, [_i32, _vp, _vp, _sz, _vp])
 _sig("qgemm_workspace_size", _sz, [C.POINTER(_Weights), _i32])
+_sig("qgemm_launch_count", _i32, [C.POINTER(_Weights), _i32, C.POINTER(_i32)])
 _sig("qgemm_workspace_init", _i32, [_vp, _sz, _vp])
 _sig("qgemm_gemm_w4a16", _i32, [C.POINTER(_Weights), _vp, _i32, _vp, _vp, _sz, _vp])
 _sig("qgemm_gemm_w4a16_f32", _i32, [C.POINTER(_Weights), _vp, _i32, _vp, _vp, _sz, _vp])
@@ -279,6 +280,19 @@ def codec_encode(kind: str, x: torch.Tensor, stream=None) -> torch.Tensor:
 def workspace_size(p: Packed, M: int) -> int:
     d = p.desc()
     return _lib.qgemm_workspace_size(C.byref(d), M)
+
+
+KERNEL_NAMES = {0: "k_gemv", 1: "k_gemv_tma", 2: "k_umma_sk", 3: "k_umma_ts"}
+
+
+def launch_count(p: Packed, M: int) -> tuple[int, str]:
+    """(kernel launches one gemm_w4a16 call makes, name of its GEMM kernel)."""
+    d = p.desc()
+    k = _i32(0)
+    n = _lib.qgemm_launch_count(C.byref(d), M, C.byref(k))
+    if n < 0:
+        raise QGemmError(-1, "launch_count: invalid arguments")
+    return n, KERNEL_NAMES[k.value]
 
 
 def make_workspace(p: Packed, M: int, stream=None) -> torch.Tensor:

@@ -631,6 +631,21 @@ size_t gemm_decode_workspace(const qgemm_weights_t* w, int M) {
   return need;
 }
 
+// Mirrors gemm_decode's dispatch: launches per call and the GEMM kernel used.
+int32_t gemm_launch_count(const qgemm_weights_t* w, int M, int32_t* kernel) {
+  if (!w || M < 1 || fmt_code(w->format) < 0) return -1;
+  int k = 0, n = 0;
+  if (use_umma(w, M)) {
+    k = umma_sk_supported(w, M) ? 2 : 3;
+    n = 2;  // k_xprep + the tcgen05 kernel
+  } else {
+    k = gemv_tma_supported(w, M < kMaxM ? M : kMaxM) ? 1 : 0;
+    n = 2 * ((M + kMaxM - 1) / kMaxM);  // per 16 activation rows: k_xprep + decode kernel
+  }
+  if (kernel) *kernel = k;
+  return n;
+}
+
 }  // namespace qg
 
 using namespace qg;
@@ -638,6 +653,10 @@ using namespace qg;
 extern "C" {
 
 size_t qgemm_workspace_size(const qgemm_weights_t* w, int32_t M) { return gemm_decode_workspace(w, M); }
+
+int32_t qgemm_launch_count(const qgemm_weights_t* w, int32_t M, int32_t* kernel) {
+  return gemm_launch_count(w, M, kernel);
+}
 
 qgemm_status_t qgemm_workspace_init(void* ws, size_t ws_bytes, void* stream) {
   if (!ws && ws_bytes) return fail(QGEMM_ERR_INVALID_ARG, "workspace_init: null pointer");
