@@ -7,8 +7,10 @@ packed on the device.  One step = the 12 GEMMs, ordered M-major so that each
 call is L2-cold: between two uses of any layer at least 170 MB of other
 weights stream through the 126 MB L2, and the step's working set (419 MB of
 packed weights) exceeds L2.  With --gpus N each rank owns N/world contiguous
-rows of every W (and its scales), computes its Y slice and an NCCL all-gather
-(then a re-layout for M > 1) assembles Y; the step time is the max over ranks.
+rows of every W (and its scales), and qgemm_tp_gemm_w4a16 computes its Y
+slice and writes it into every rank's full Y over NVLink peer memory (CUDA
+IPC mappings), then waits for the other slices; the step time is the max
+over ranks (NCCL carries only barriers and the max reduction).
 
   value   Sum_calls total_bytes(MXFP4, M, N/world, K) over all ranks / step
           time (formats.cuh:80-83 accounting), device-resident inputs, each
@@ -367,36 +369,55 @@ def main():
     X = {(M, K): torch.randn((M, K), generator=gen, device=dev).to(torch.bfloat16) for M in ms for K in Kset}
     Y = {(M, name): torch.empty((M, N // world), dtype=torch.bfloat16, device=dev)
          for M in ms for name, N, _ in layers}
-    Yfull = {(M, name): torch.empty((M, N), dtype=torch.bfloat16, device=dev)
-             for M in ms for name, N, _ in layers} if world > 1 else {}
-    Ygath = {(M, name): torch.empty((world, M, N // world), dtype=torch.bfloat16, device=dev)
-             for M in ms for name, N, _ in layers if M > 1} if world > 1 else {}
     ws = {}
     for M in ms:
         for name, N, K in layers:
             ws[(M, name)] = qg.make_workspace(shards[name], M)
-    torch.cuda.synchronize()
-
     calls = [(M, name, N, K) for M in ms for name, N, K in layers]
+
+    # ---- world > 1: every rank's Y_full buffers and sync block in one
+    # allocation shared by CUDA IPC; tp_gemm writes each slice into every
+    # rank's Y_full over NVLink and waits for the other slices -------------
+    Yfull, y_peers, sync_peers, tpws, opened = {}, {}, [], {}, []
+    if world > 1:
+        offs, off = {}, 256
+        for M, name, N, K in calls:
+            offs[(M, name)] = off
+            off += (M * N * 2 + 255) // 256 * 256
+        tpbuf = torch.zeros(off, dtype=torch.uint8, device=dev)
+        handles = [None] * world
+        dist.all_gather_object(handles, qg.ipc_handle(tpbuf))
+        bases = []
+        for r in range(world):
+            if r == rank:
+                bases.append(tpbuf.data_ptr())
+            else:
+                b0, ptr = qg.ipc_open(*handles[r])
+                opened.append(b0)
+                bases.append(ptr)
+        sync_peers = bases
+        for M, name, N, K in calls:
+            o = offs[(M, name)]
+            y_peers[(M, name)] = [b + o for b in bases]
+            Yfull[(M, name)] = tpbuf[o:o + M * N * 2].view(torch.bfloat16).view(M, N)
+            tpws[(M, name)] = qg.make_tp_workspace(shards[name], M)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()  # every rank's buffers exist before any rank's first tp_gemm
     kernel_of = {(M, name): qg.launch_count(shards[name], M)[1] for M, name, N, K in calls}
     launches_per_step = sum(qg.launch_count(shards[name], M)[0] for M, name, N, K in calls)
     bytes_rank = sum(qg.total_bytes(fcode, M, N // world, K) for M, name, N, K in calls)
     bytes_step = bytes_rank * world
 
-    def gather(M, name):
+    def gemm(M, name, Xin):
         if world == 1:
-            return
-        if M == 1:
-            dist.all_gather_into_tensor(Yfull[(M, name)].view(-1), Y[(M, name)].view(-1))
+            qg.gemm_w4a16(shards[name], Xin, out=Y[(M, name)], workspace=ws[(M, name)])
         else:
-            g = Ygath[(M, name)]
-            dist.all_gather_into_tensor(g.view(-1), Y[(M, name)].view(-1))
-            Yfull[(M, name)].view(M, world, -1).copy_(g.permute(1, 0, 2))
+            qg.tp_gemm(shards[name], Xin, world, rank, y_peers[(M, name)], sync_peers, tpws[(M, name)])
 
     def step():
         for M, name, N, K in calls:
-            qg.gemm_w4a16(shards[name], X[(M, K)], out=Y[(M, name)], workspace=ws[(M, name)])
-            gather(M, name)
+            gemm(M, name, X[(M, K)])
 
     s = torch.cuda.Stream(device=dev)
     s.wait_stream(torch.cuda.current_stream())
@@ -425,6 +446,7 @@ def main():
         ev1.record()
         torch.cuda.synchronize()
     if world > 1:
+        qg.tp_status()
         dist.barrier()
     ms_step = ev0.elapsed_time(ev1) / args.steps
     t = torch.tensor([ms_step], device=dev)
@@ -451,8 +473,7 @@ def main():
         for key in Xd:
             Xd[key].copy_(Xh[key], non_blocking=True)
         for M, name, N, K in calls:
-            qg.gemm_w4a16(shards[name], Xd[(M, K)], out=Y[(M, name)], workspace=ws[(M, name)])
-            gather(M, name)
+            gemm(M, name, Xd[(M, K)])
             done[(M, name)].record(main)
             cs.wait_event(done[(M, name)])
             with torch.cuda.stream(cs):
@@ -561,7 +582,8 @@ def main():
             "data": "synthetic (seeded N(0,1) X, N(0,0.02) W packed on device)",
             "config": {"workload": args.workload, "format": fmt,
                        "layers": [[n, N, K] for n, N, K in layers], "M": ms,
-                       "parallelism": f"N-shard x{world}" + (" + NCCL all-gather" if world > 1 else ""),
+                       "parallelism": f"N-shard x{world}" + (" + all-gather of Y over NVLink peer stores "
+                                                              "(qgemm_tp_gemm_w4a16)" if world > 1 else ""),
                        "l2": "cold: step working set 419 MB > 126 MB L2, calls M-major",
                        "pct_of_hbm_peak": round(100 * value / peak, 2)},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d * world,
@@ -583,8 +605,12 @@ def main():
         }
         print(json.dumps(line), flush=True)
     if world > 1:
+        torch.cuda.synchronize()
+        qg.tp_status()
         del graph
-        dist.barrier()
+        dist.barrier()  # no rank unmaps while a peer may still write into it
+        for b0 in opened:
+            qg.ipc_close(b0)
         dist.destroy_process_group()
 
 

@@ -137,6 +137,36 @@ qgemm_status_t qgemm_gemm_w4a16_f32(const qgemm_weights_t* w, const uint16_t* X,
                                     int32_t M, float* Y, void* workspace,
                                     size_t ws_bytes, void* stream);
 
+/* ---- tensor parallel over the GPUs of one node (W sharded along N) -------
+ * No counterpart in the reference, which runs on one GPU; the sharding
+ * (rank r holds rows [r N/world, (r+1) N/world) of W and its scales) and the
+ * gather of Y are the multi-GPU step its bench is extended with.
+ * qgemm_tp_gemm_w4a16 computes this rank's Y slice with qgemm_gemm_w4a16's
+ * kernels, writes it into every rank's Y_full [M][N] through peer pointers
+ * (y_peers[d] = rank d's Y_full as mapped in this process), then announces
+ * the call in every rank's sync block and waits (bounded, 2 s) until all
+ * ranks' slices have landed in its own Y_full.  Every rank makes the same
+ * sequence of calls; a rank's Y_full is written by all ranks, so reuse a
+ * buffer only once every rank is done reading the previous result.
+ * sync_peers[d]: rank d's sync block, qgemm_tp_sync_bytes() bytes, zeroed
+ * once.  workspace: qgemm_tp_workspace_size(w_local, M) bytes, zeroed once
+ * (qgemm_workspace_init).  Graph-capturable: the call's sequence number is
+ * a device-side counter in the sync block. */
+size_t qgemm_tp_sync_bytes(int32_t world);
+size_t qgemm_tp_workspace_size(const qgemm_weights_t* w_local, int32_t M);
+qgemm_status_t qgemm_tp_gemm_w4a16(const qgemm_weights_t* w_local, const uint16_t* X,
+                                   int32_t M, int32_t world, int32_t rank,
+                                   uint16_t* const* y_peers, uint32_t* const* sync_peers,
+                                   void* workspace, size_t ws_bytes, void* stream);
+/* QGEMM_ERR_TIMEOUT if a tp wait gave up (a peer never announced). */
+qgemm_status_t qgemm_tp_status(int32_t* timed_out);
+/* CUDA IPC: the 64-byte handle of the allocation holding dev_ptr and the
+ * pointer's byte offset in it; mapping another process's allocation from
+ * its handle (*dev_ptr = its base, add the offset) and unmapping it. */
+qgemm_status_t qgemm_ipc_handle(const void* dev_ptr, uint8_t* handle64, size_t* offset);
+qgemm_status_t qgemm_ipc_open(const uint8_t* handle64, void** dev_ptr);
+qgemm_status_t qgemm_ipc_close(void* dev_ptr);
+
 /* Y = X . W^T (bf16 out) without a workspace argument, for callers that
  * cannot provide one: an operator slot that passes only inputs, outputs and a
  * stream, a plugin inside a framework that owns the device memory pool and

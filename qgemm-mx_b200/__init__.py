@@ -78,6 +78,14 @@ _sig("qgemm_probe_launch", _i32, [_i32, _vp, _vp, _sz, _vp])
 _sig("qgemm_device_info", _i32, [C.POINTER(_i32), C.POINTER(_sz)])
 _sig("qgemm_probe_status", _i32, [C.POINTER(_i32)])
 _sig("qgemm_umma_status", _i32, [C.POINTER(_i32)])
+_sig("qgemm_tp_sync_bytes", _sz, [_i32])
+_sig("qgemm_tp_workspace_size", _sz, [C.POINTER(_Weights), _i32])
+_sig("qgemm_tp_gemm_w4a16", _i32, [C.POINTER(_Weights), C.c_void_p, _i32, _i32, _i32, C.POINTER(C.c_void_p),
+                                   C.POINTER(C.c_void_p), C.c_void_p, _sz, C.c_void_p])
+_sig("qgemm_tp_status", _i32, [C.POINTER(_i32)])
+_sig("qgemm_ipc_handle", _i32, [C.c_void_p, C.POINTER(C.c_uint8), C.POINTER(_sz)])
+_sig("qgemm_ipc_open", _i32, [C.POINTER(C.c_uint8), C.POINTER(C.c_void_p)])
+_sig("qgemm_ipc_close", _i32, [C.c_void_p])
 
 EXPORTED = [n for n in dir(_lib) if n.startswith("qgemm_")]
 
@@ -344,6 +352,61 @@ def umma_status() -> None:
     """Raises QGemmError if a bounded wait inside the tcgen05 kernel gave up."""
     f = _i32(0)
     _check(_lib.qgemm_umma_status(C.byref(f)), "umma_status")
+
+
+# ---- tensor parallel (W sharded along N over the GPUs of one node) ------------
+
+def tp_sync_bytes(world: int) -> int:
+    return _lib.qgemm_tp_sync_bytes(world)
+
+
+def make_tp_workspace(p: Packed, M: int, stream=None) -> torch.Tensor:
+    """Zeroed workspace for tp_gemm of this rank's shard p."""
+    d = p.desc()
+    n = max(_lib.qgemm_tp_workspace_size(C.byref(d), M), 256)
+    ws = torch.empty(n, dtype=torch.uint8, device=p.data.device)
+    _check(_lib.qgemm_workspace_init(_ptr(ws), n, _stream(stream)), "workspace_init")
+    return ws
+
+
+def tp_gemm(p: Packed, X: torch.Tensor, world: int, rank: int, y_peers: list[int], sync_peers: list[int],
+            workspace: torch.Tensor, stream=None) -> None:
+    """This rank's slice of Y = X . W^T written into every rank's Y_full
+    (y_peers[d]: rank d's Y_full [M][N] as mapped here, device addresses),
+    then a bounded wait until all ranks' slices are in this rank's Y_full."""
+    if X.dtype != torch.bfloat16 or not X.is_contiguous():
+        raise ValueError("X must be contiguous bf16")
+    d = p.desc()
+    yp = (C.c_void_p * world)(*y_peers)
+    sp = (C.c_void_p * world)(*sync_peers)
+    _check(_lib.qgemm_tp_gemm_w4a16(C.byref(d), _ptr(X), X.shape[0], world, rank, yp, sp, _ptr(workspace),
+                                    workspace.numel(), _stream(stream)), "tp_gemm")
+
+
+def tp_status() -> None:
+    """Raises QGemmError if a tp wait gave up (a peer never announced)."""
+    f = _i32(0)
+    _check(_lib.qgemm_tp_status(C.byref(f)), "tp_status")
+
+
+def ipc_handle(t: torch.Tensor) -> tuple[bytes, int]:
+    """(64-byte CUDA IPC handle of the allocation holding t, t's byte offset in it)."""
+    h = (C.c_uint8 * 64)()
+    off = _sz(0)
+    _check(_lib.qgemm_ipc_handle(_ptr(t), h, C.byref(off)), "ipc_handle")
+    return bytes(h), off.value
+
+
+def ipc_open(handle: bytes, offset: int) -> tuple[int, int]:
+    """Maps another process's allocation; returns (base to close later, address of the shared pointer)."""
+    h = (C.c_uint8 * 64)(*handle)
+    ptr = C.c_void_p(0)
+    _check(_lib.qgemm_ipc_open(h, C.byref(ptr)), "ipc_open")
+    return ptr.value, ptr.value + offset
+
+
+def ipc_close(base: int) -> None:
+    _check(_lib.qgemm_ipc_close(C.c_void_p(base)), "ipc_close")
 
 
 def device_info() -> tuple[int, int]:

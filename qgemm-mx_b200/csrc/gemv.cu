@@ -50,6 +50,7 @@
 
 #include "common.cuh"
 #include "gemv_core.cuh"
+#include "tp.cuh"
 
 namespace qg {
 
@@ -489,13 +490,13 @@ bool umma_sk_supported(const qgemm_weights_t* w, int M);
 int umma_sk_bn(int M);
 size_t umma_sk_workspace(const qgemm_weights_t* w, int M, int sm_count);
 qgemm_status_t gemm_umma_sk(const qgemm_weights_t* w, const __half* Xh, const float* xs, int M, void* Y, bool f32,
-                            void* ws, int sm_count, cudaStream_t s);
+                            void* ws, int sm_count, cudaStream_t s, const TpOut* tp);
 
 bool gemv_tma_supported(const qgemm_weights_t* w, int mb);
 size_t gemv_tma_workspace(const qgemm_weights_t* w, int sm_count);
 size_t gemv_tma_xg_offset(const qgemm_weights_t* w, int sm_count);
 qgemm_status_t gemm_gemv_tma(const qgemm_weights_t* w, const __half* xg, const float* xs, int mb, void* Y, int ldy,
-                             bool f32, void* ws, int sm_count, cudaStream_t s);
+                             bool f32, void* ws, int sm_count, cudaStream_t s, const TpOut* tp);
 // [xs (16 floats) | counters | partials | X image]
 static size_t decode_tma_workspace(const qgemm_weights_t* w, int sms) {
   return pad256((size_t)kMaxM * sizeof(float)) + gemv_tma_workspace(w, sms);
@@ -531,9 +532,11 @@ static size_t umma_workspace(const qgemm_weights_t* w, int M) {
   return head + umma_split_workspace(w, M, umma_split_count(w, M));
 }
 
-qgemm_status_t gemm_decode(const qgemm_weights_t* w, const uint16_t* X, int M, void* Y, bool f32, void* ws,
-                           size_t ws_bytes, cudaStream_t s) {
-  if (!w || !X || !Y) return fail(QGEMM_ERR_INVALID_ARG, "gemm: null pointer");
+// tp: tensor-parallel output (kernels that write every rank's Y_full); only
+// with the TMA-fed decode and stream-K tcgen05 kernels, Y unused then.
+qgemm_status_t gemm_decode_ex(const qgemm_weights_t* w, const uint16_t* X, int M, void* Y, bool f32, void* ws,
+                              size_t ws_bytes, cudaStream_t s, const TpOut* tp) {
+  if (!w || !X || (!Y && !tp)) return fail(QGEMM_ERR_INVALID_ARG, "gemm: null pointer");
   if (M < 1) return fail(QGEMM_ERR_INVALID_ARG, "gemm: M must be >= 1");
   if (!w->data || !w->scales) return fail(QGEMM_ERR_INVALID_ARG, "gemm: null weight pointer");
   if (w->reserved != 0) return fail(QGEMM_ERR_INVALID_ARG, "gemm: reserved field must be 0");
@@ -558,8 +561,9 @@ qgemm_status_t gemm_decode(const qgemm_weights_t* w, const uint16_t* X, int M, v
       const int bn = umma_sk_bn(M);
       k_xprep<<<(M + bn - 1) / bn * bn, 256, 0, s>>>(X, M, (int)w->K, 0, 1, bn, xh, xs);
       QG_LAUNCH_RET();
-      return gemm_umma_sk(w, xh, xs, M, Y, f32, split_ws, sm_count_or_zero(), s);
+      return gemm_umma_sk(w, xh, xs, M, Y, f32, split_ws, sm_count_or_zero(), s, tp);
     }
+    if (tp) return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "gemm: no tensor-parallel output on this path");
     k_xprep<<<M, 256, 0, s>>>(X, M, (int)w->K, 0, 0, 0, xh, xs);
     QG_LAUNCH_RET();
     return gemm_umma_ts(w, xh, xs, M, Y, f32, umma_split_count(w, M), split_ws, s);
@@ -579,13 +583,20 @@ qgemm_status_t gemm_decode(const qgemm_weights_t* w, const uint16_t* X, int M, v
       const int mpad = mb <= 8 ? 8 : 16;
       k_xprep<<<mpad, 256, 0, s>>>(X + (size_t)m0 * w->K, mb, (int)w->K, 0, 2, mpad, xg, xs);
       QG_LAUNCH_RET();
-      void* Yb = f32 ? (void*)(static_cast<float*>(Y) + (size_t)m0 * w->N)
-                     : (void*)(static_cast<uint16_t*>(Y) + (size_t)m0 * w->N);
-      st = gemm_gemv_tma(w, xg, xs, mb, Yb, (int)w->N, f32, tws, sms, s);
+      if (tp) {  // this block's rows of every rank's Y_full
+        TpOut tb = *tp;
+        for (int d = 0; d < tb.world; ++d) tb.y[d] += (size_t)m0 * tb.ldy;
+        st = gemm_gemv_tma(w, xg, xs, mb, nullptr, 0, false, tws, sms, s, &tb);
+      } else {
+        void* Yb = f32 ? (void*)(static_cast<float*>(Y) + (size_t)m0 * w->N)
+                       : (void*)(static_cast<uint16_t*>(Y) + (size_t)m0 * w->N);
+        st = gemm_gemv_tma(w, xg, xs, mb, Yb, (int)w->N, f32, tws, sms, s, nullptr);
+      }
       if (st != QGEMM_OK) return st;
     }
     return QGEMM_OK;
   }
+  if (tp) return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "gemm: no tensor-parallel output on this path");
   if (!ws || !al16(ws) || ws_bytes < p.total())
     return fail(QGEMM_ERR_WORKSPACE, "gemm: 16-byte aligned workspace of %zu bytes needed, %zu given", p.total(),
                 ws_bytes);
@@ -613,6 +624,11 @@ qgemm_status_t gemm_decode(const qgemm_weights_t* w, const uint16_t* X, int M, v
     if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "gemm: launch failed: %s", cudaGetErrorString(e));
   }
   return QGEMM_OK;
+}
+
+qgemm_status_t gemm_decode(const qgemm_weights_t* w, const uint16_t* X, int M, void* Y, bool f32, void* ws,
+                           size_t ws_bytes, cudaStream_t s) {
+  return gemm_decode_ex(w, X, M, Y, f32, ws, ws_bytes, s, nullptr);
 }
 
 size_t gemm_decode_workspace(const qgemm_weights_t* w, int M) {

@@ -35,6 +35,7 @@
 #include "common.cuh"
 #include "gemv_core.cuh"
 #include "tc.cuh"
+#include "tp.cuh"
 
 namespace qg {
 
@@ -76,6 +77,7 @@ struct GtArgs {
   int KS;                // units per tile (K / 256)
   int G;
   float ts;
+  TpOut tp;              // world > 0: store into every rank's Y_full, then tp_finish
 };
 
 template <int FMT, int NT, bool F32OUT>
@@ -200,6 +202,7 @@ k_gemv_tma(const __grid_constant__ CUtensorMap map_w, const GtArgs a) {
             float y = v[0][t][e] * __ldg(a.xs + m);
             if (FMT == 1) y *= a.ts;
             if (F32OUT) static_cast<float*>(a.Y)[(size_t)m * a.ldy + n] = y;
+            else if (a.tp.world > 0) tp_store(a.tp, (size_t)m, n, __float2bfloat16_rn(y));
             else static_cast<__nv_bfloat16*>(a.Y)[(size_t)m * a.ldy + n] = __float2bfloat16_rn(y);
           }
         }
@@ -334,6 +337,7 @@ k_gemv_tma(const __grid_constant__ CUtensorMap map_w, const GtArgs a) {
     }
   }
   __syncthreads();
+  if (a.tp.world > 0) tp_finish(a.tp, fault);
 }
 
 // ---------------------------------------------------------------------------
@@ -403,7 +407,7 @@ static cudaError_t launch_gt_t(const CUtensorMap& mw, const GtArgs& a, cudaStrea
 // k_xprep, mpad = 8 * ceil(mb / 8)) and row factors are already in xg / xs.
 // ws: gemv_tma_workspace bytes, counters zero.
 qgemm_status_t gemm_gemv_tma(const qgemm_weights_t* w, const __half* xg, const float* xs, int mb, void* Y, int ldy,
-                             bool f32, void* ws, int sm_count, cudaStream_t s) {
+                             bool f32, void* ws, int sm_count, cudaStream_t s, const TpOut* tp) {
   if (!gemv_tma_supported(w, mb)) return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "TMA decode path: unsupported shape");
   if (sm_count <= 0) return fail(QGEMM_ERR_CUDA, "TMA decode path: no device properties");
   const GtPlan p = gt_plan(w, mb, sm_count);
@@ -420,6 +424,11 @@ qgemm_status_t gemm_gemv_tma(const qgemm_weights_t* w, const __half* xg, const f
   a.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + p.counter_bytes);
   a.T = p.T; a.M = mb; a.N = (int)w->N; a.K = (int)w->K; a.ldy = ldy;
   a.KS = p.KS; a.G = p.G; a.ts = w->tensor_scale;
+  a.tp = {};
+  if (tp) {
+    if (f32) return fail(QGEMM_ERR_INVALID_ARG, "TMA decode path: tensor-parallel output is bf16");
+    a.tp = *tp;
+  }
   cudaError_t e;
   if (w->format == QGEMM_FMT_MXFP4) {
     if (p.nt == 1) e = f32 ? launch_gt_t<0, 1, true>(mw, a, s) : launch_gt_t<0, 1, false>(mw, a, s);

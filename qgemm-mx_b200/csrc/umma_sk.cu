@@ -61,6 +61,7 @@
 
 #include "common.cuh"
 #include "tc.cuh"
+#include "tp.cuh"
 
 namespace qg {
 
@@ -107,6 +108,7 @@ struct SkArgs {
   int KS;               // steps per tile (K / 128)
   int G;                // CTAs
   float ts;
+  TpOut tp;             // world > 0: store into every rank's Y_full, then tp_finish
 };
 
 // Largest E8M0 byte among nbytes scale bytes at p, with NaN codes (0xFF)
@@ -445,6 +447,7 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
                 if (m < a.M) {
                   const float y = u2f(v[u]) * rowf * __ldg(a.xs + m);
                   if (F32OUT) static_cast<float*>(a.Y)[(size_t)m * a.N + n] = y;
+                  else if (a.tp.world > 0) tp_store(a.tp, (size_t)m, n, __float2bfloat16_rn(y));
                   else static_cast<__nv_bfloat16*>(a.Y)[(size_t)m * a.N + n] = __float2bfloat16_rn(y);
                 }
               }
@@ -497,6 +500,7 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
                 if (m < a.M) {
                   const float y = acc[u] * __ldg(a.xs + m);
                   if (F32OUT) static_cast<float*>(a.Y)[(size_t)m * a.N + n] = y;
+                  else if (a.tp.world > 0) tp_store(a.tp, (size_t)m, n, __float2bfloat16_rn(y));
                   else static_cast<__nv_bfloat16*>(a.Y)[(size_t)m * a.N + n] = __float2bfloat16_rn(y);
                 }
               }
@@ -524,6 +528,7 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512u));
   }
+  if (a.tp.world > 0) tp_finish(a.tp, fault);
 }
 
 // ---------------------------------------------------------------------------
@@ -600,7 +605,7 @@ static cudaError_t launch_sk_bn(int bn, const CUtensorMap& mw, const SkArgs& a, 
 // factors (k_xprep with swz_bn = umma_sk_bn(M)); ws: the
 // counters + partials block of umma_sk_workspace bytes (counters zero).
 qgemm_status_t gemm_umma_sk(const qgemm_weights_t* w, const __half* Xh, const float* xs, int M, void* Y, bool f32,
-                            void* ws, int sm_count, cudaStream_t s) {
+                            void* ws, int sm_count, cudaStream_t s, const TpOut* tp) {
   if (!umma_sk_supported(w, M)) return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "stream-K tcgen05 path: unsupported shape");
   if (sm_count <= 0) return fail(QGEMM_ERR_CUDA, "stream-K tcgen05 path: no device properties");
   const SkPlan p = sk_plan(w, M, sm_count);
@@ -616,6 +621,11 @@ qgemm_status_t gemm_umma_sk(const qgemm_weights_t* w, const __half* Xh, const fl
   a.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + p.counter_bytes);
   a.T = p.T; a.M = M; a.N = (int)w->N; a.K = (int)w->K;
   a.tiles_n = p.tiles_n; a.KS = p.KS; a.G = p.G; a.ts = w->tensor_scale;
+  a.tp = {};
+  if (tp) {
+    if (f32) return fail(QGEMM_ERR_INVALID_ARG, "stream-K tcgen05 path: tensor-parallel output is bf16");
+    a.tp = *tp;
+  }
   cudaError_t e;
   if (w->format == QGEMM_FMT_MXFP4)
     e = f32 ? launch_sk_bn<0, true>(p.bn, mw, a, s) : launch_sk_bn<0, false>(p.bn, mw, a, s);
