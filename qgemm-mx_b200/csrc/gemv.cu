@@ -102,35 +102,74 @@ __device__ __forceinline__ size_t xprep_index(int m, int k, int K, int layout, i
   const int pos = (c & ~7) | ((c ^ m) & 7);
   return (((size_t)u * lp + m) * 32 + pos) * 8;
 }
-__global__ void __launch_bounds__(256) k_xprep(const uint16_t* __restrict__ X, int M, int K, int perm, int layout,
-                                               int lp, __half* __restrict__ Xh, float* __restrict__ xs) {
+// One pass: every thread issues all its 16-byte loads of the row before it
+// uses any (up to kXpChunks of them, i.e. K <= 256 * 8 * kXpChunks), keeps
+// them in registers for the block-wide |x| maximum and converts from there;
+// longer rows load the remainder again for the conversion.  Launched as a
+// programmatic dependent: it waits for the previous grid before reading X
+// (which that grid may have produced) or writing Xh / xs (which it may read).
+constexpr int kXpThreads = 256;
+constexpr int kXpChunks = 16;
+__device__ __forceinline__ void xprep_store(const uint4 v, float inv, int perm, __half* dst) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  float f[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = u2f(w[i] << 16) * inv;
+    f[2 * i + 1] = u2f(w[i] & 0xFFFF0000u) * inv;
+  }
+  __half2 o[4];
+  if (perm) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[i] = __floats2half2_rn(f[i], f[i + 4]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[i] = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+  }
+  *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(o);
+}
+__device__ __forceinline__ float absmax8(const uint4 v, float a) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    a = fmaxf(a, fabsf(u2f(w[i] << 16)));
+    a = fmaxf(a, fabsf(u2f(w[i] & 0xFFFF0000u)));
+  }
+  return a;
+}
+__global__ void __launch_bounds__(kXpThreads) k_xprep(const uint16_t* __restrict__ X, int M, int K, int perm,
+                                                      int layout, int lp, __half* __restrict__ Xh,
+                                                      float* __restrict__ xs) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;");
   const int m = blockIdx.x;
+  constexpr int kStride = kXpThreads * 8;
   if (m >= M) {  // zero padding rows of the last activation block
-    for (int k = threadIdx.x * 8; k < K; k += blockDim.x * 8)
+    for (int k = threadIdx.x * 8; k < K; k += kStride)
       *reinterpret_cast<uint4*>(Xh + xprep_index(m, k, K, layout, lp)) = make_uint4(0u, 0u, 0u, 0u);
     return;
   }
-  __shared__ float red[8];
+  __shared__ float red[kXpThreads / 32];
   __shared__ float s_inv;
   const uint16_t* xr = X + (size_t)m * K;
-  float amax = 0.0f;
-  for (int k = threadIdx.x * 8; k < K; k += blockDim.x * 8) {
-    const uint4 v = *reinterpret_cast<const uint4*>(xr + k);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint4 v[kXpChunks];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      amax = fmaxf(amax, fabsf(u2f(w[i] << 16)));
-      amax = fmaxf(amax, fabsf(u2f(w[i] & 0xFFFF0000u)));
-    }
+  for (int i = 0; i < kXpChunks; ++i) {
+    const int k = threadIdx.x * 8 + i * kStride;
+    v[i] = k < K ? *reinterpret_cast<const uint4*>(xr + k) : make_uint4(0u, 0u, 0u, 0u);
   }
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kXpChunks; ++i) amax = absmax8(v[i], amax);
+  for (int k = threadIdx.x * 8 + kXpChunks * kStride; k < K; k += kStride)
+    amax = absmax8(*reinterpret_cast<const uint4*>(xr + k), amax);
 #pragma unroll
   for (int d = 16; d; d >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, d));
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
   __syncthreads();
   if (threadIdx.x == 0) {
     float a = 0.0f;
-    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) a = fmaxf(a, red[i]);
+    for (int i = 0; i < kXpThreads / 32; ++i) a = fmaxf(a, red[i]);
     int s = 0;
     if (a > 0.0f && isfinite(a)) {
       s = ilogbf(a) - 14;
@@ -141,25 +180,28 @@ __global__ void __launch_bounds__(256) k_xprep(const uint16_t* __restrict__ X, i
   }
   __syncthreads();
   const float inv = s_inv;
-  for (int k = threadIdx.x * 8; k < K; k += blockDim.x * 8) {
-    const uint4 v = *reinterpret_cast<const uint4*>(xr + k);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-    float f[8];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      f[2 * i] = u2f(w[i] << 16) * inv;
-      f[2 * i + 1] = u2f(w[i] & 0xFFFF0000u) * inv;
-    }
-    __half2 o[4];
-    if (perm) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) o[i] = __floats2half2_rn(f[i], f[i + 4]);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) o[i] = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
-    }
-    *reinterpret_cast<uint4*>(Xh + xprep_index(m, k, K, layout, lp)) = *reinterpret_cast<const uint4*>(o);
+  for (int i = 0; i < kXpChunks; ++i) {
+    const int k = threadIdx.x * 8 + i * kStride;
+    if (k < K) xprep_store(v[i], inv, perm, Xh + xprep_index(m, k, K, layout, lp));
   }
+  for (int k = threadIdx.x * 8 + kXpChunks * kStride; k < K; k += kStride)
+    xprep_store(*reinterpret_cast<const uint4*>(xr + k), inv, perm, Xh + xprep_index(m, k, K, layout, lp));
+}
+
+// PDL launch of k_xprep over `rows` CTAs (rows >= M: the extra rows are zeroed).
+static cudaError_t launch_xprep(const uint16_t* X, int M, int rows, int K, int perm, int layout, int lp, __half* Xh,
+                                float* xs, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)rows);
+  cfg.blockDim = dim3(kXpThreads);
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_xprep, X, M, K, perm, layout, lp, Xh, xs);
 }
 
 // ---------------------------------------------------------------------------
@@ -503,7 +545,7 @@ static size_t decode_tma_workspace(const qgemm_weights_t* w, int sms) {
 }
 
 // The tcgen05 paths (dequantised W in TMEM) take MXFP4 / NVFP4 with M >= 32:
-// the persistent stream-K kernel for M < 256 and K % 128 == 0 (umma_sk.cu),
+// the persistent stream-K kernel for M < 128 and K % 256 == 0 (umma_sk.cu),
 // the tile-per-CTA kernel with K splits otherwise (K % 64 == 0, umma.cu).
 // Their workspace holds the f16 copy of X, its row factors and the split
 // tiles' tickets and partial sums.
@@ -559,13 +601,11 @@ qgemm_status_t gemm_decode_ex(const qgemm_weights_t* w, const uint16_t* X, int M
     void* split_ws = static_cast<uint8_t*>(ws) + pad256((size_t)M * sizeof(float)) + umma_xh_bytes(w, M);
     if (umma_sk_supported(w, M)) {
       const int bn = umma_sk_bn(M);
-      k_xprep<<<(M + bn - 1) / bn * bn, 256, 0, s>>>(X, M, (int)w->K, 0, 1, bn, xh, xs);
-      QG_LAUNCH_RET();
+      QG_CUDA_RET(launch_xprep(X, M, (M + bn - 1) / bn * bn, (int)w->K, 0, 1, bn, xh, xs, s));
       return gemm_umma_sk(w, xh, xs, M, Y, f32, split_ws, sm_count_or_zero(), s, tp);
     }
     if (tp) return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "gemm: no tensor-parallel output on this path");
-    k_xprep<<<M, 256, 0, s>>>(X, M, (int)w->K, 0, 0, 0, xh, xs);
-    QG_LAUNCH_RET();
+    QG_CUDA_RET(launch_xprep(X, M, M, (int)w->K, 0, 0, 0, xh, xs, s));
     return gemm_umma_ts(w, xh, xs, M, Y, f32, umma_split_count(w, M), split_ws, s);
   }
   if (gemv_tma_supported(w, M < kMaxM ? M : kMaxM)) {
@@ -581,8 +621,7 @@ qgemm_status_t gemm_decode_ex(const qgemm_weights_t* w, const uint16_t* X, int M
     for (int m0 = 0; m0 < M; m0 += kMaxM) {
       const int mb = (M - m0) < kMaxM ? (M - m0) : kMaxM;
       const int mpad = mb <= 8 ? 8 : 16;
-      k_xprep<<<mpad, 256, 0, s>>>(X + (size_t)m0 * w->K, mb, (int)w->K, 0, 2, mpad, xg, xs);
-      QG_LAUNCH_RET();
+      QG_CUDA_RET(launch_xprep(X + (size_t)m0 * w->K, mb, mpad, (int)w->K, 0, 2, mpad, xg, xs, s));
       if (tp) {  // this block's rows of every rank's Y_full
         TpOut tb = *tp;
         for (int d = 0; d < tb.world; ++d) tb.y[d] += (size_t)m0 * tb.ldy;
@@ -618,8 +657,7 @@ qgemm_status_t gemm_decode_ex(const qgemm_weights_t* w, const uint16_t* X, int M
     a.T = pb.T; a.C = pb.C; a.W_total = pb.W_total; a.M = mb;
     a.Y = f32 ? (void*)(static_cast<float*>(Y) + (size_t)m0 * w->N)
               : (void*)(static_cast<uint16_t*>(Y) + (size_t)m0 * w->N);
-    k_xprep<<<mb, 256, 0, s>>>(X + (size_t)m0 * w->K, mb, (int)w->K, perm, 0, 0, xh, xs);
-    QG_LAUNCH_RET();
+    QG_CUDA_RET(launch_xprep(X + (size_t)m0 * w->K, mb, mb, (int)w->K, perm, 0, 0, xh, xs, s));
     const cudaError_t e = f32 ? launch_gemv<true>(pb, a, s) : launch_gemv<false>(pb, a, s);
     if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "gemm: launch failed: %s", cudaGetErrorString(e));
   }
@@ -779,8 +817,7 @@ extern "C" qgemm_status_t qgemm_gemm_w4a16_noalloc(const qgemm_weights_t* w, con
     if (st != QGEMM_OK) return st;
     a.T = pb.T; a.C = pb.C; a.W_total = pb.W_total; a.M = mb;
     a.Y = static_cast<uint16_t*>(Y) + (size_t)m0 * w->N;
-    k_xprep<<<mb, 256, 0, s>>>(X + (size_t)m0 * w->K, mb, (int)w->K, perm, 0, 0, xh, xs);
-    QG_LAUNCH_RET();
+    QG_CUDA_RET(launch_xprep(X + (size_t)m0 * w->K, mb, mb, (int)w->K, perm, 0, 0, xh, xs, s));
     const cudaError_t e = launch_gemv<false>(pb, a, s);
     if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "gemm_noalloc: launch failed: %s", cudaGetErrorString(e));
   }

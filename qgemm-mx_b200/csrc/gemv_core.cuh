@@ -134,10 +134,28 @@ template <int FMT, int R, int NT>
 __device__ __forceinline__ void chunk_mma(float (&acc)[R][NT][4], const uint32_t (&cw)[R][2][4],
                                           const uint32_t (&cs)[R][2], const uint32_t (&cx)[NT][16]) {
   if constexpr (FMT == 0) {
-    // block b of the chunk = MMAs (b,0), (b,1); post-scale by 2^(e8m0-127)
-    bool special[R];
+    // block b of the chunk = MMAs (b,0), (b,1); post-scale by 2^(e8m0-127).
+    // The chunk's 8 R scales are decoded before the MMA loop so that loop is
+    // straight-line code; a 0x00 (2^-127) or 0xFF (NaN) byte anywhere in the
+    // warp's chunk sends the whole warp through the exact decoder once.
+    float sc[R][2][4];
+    bool special = false;
 #pragma unroll
-    for (int r = 0; r < R; ++r) special[r] = has_00_or_ff(cs[r][0]) || has_00_or_ff(cs[r][1]);
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        special |= has_00_or_ff(cs[r][h]);
+#pragma unroll
+        for (int b = 0; b < 4; ++b) sc[r][h][b] = e8m0_fast(cs[r][h], b);
+      }
+    if (__any_sync(0xFFFFFFFFu, special)) {
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int b = 0; b < 4; ++b) sc[r][h][b] = e8m0_decode((cs[r][h] >> (8 * b)) & 0xFFu);
+    }
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
       uint32_t A[R][2][4];
@@ -147,11 +165,7 @@ __device__ __forceinline__ void chunk_mma(float (&acc)[R][NT][4], const uint32_t
         for (int h = 0; h < 2; ++h) e2m1x8_to_f16(cw[r][h][b], A[r][h]);
 #pragma unroll
       for (int r = 0; r < R; ++r) {
-        float s0 = e8m0_fast(cs[r][0], b), s1 = e8m0_fast(cs[r][1], b);
-        if (special[r]) {  // a 0x00 (2^-127) or 0xFF (NaN) scale in this chunk
-          s0 = e8m0_decode(cs[r][0] >> (8 * b));
-          s1 = e8m0_decode(cs[r][1] >> (8 * b));
-        }
+        const float s0 = sc[r][0][b], s1 = sc[r][1][b];
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
           float tmp[4];
@@ -165,16 +179,24 @@ __device__ __forceinline__ void chunk_mma(float (&acc)[R][NT][4], const uint32_t
       }
     }
   } else if constexpr (FMT == 1) {
-    // words 0,1 -> block 2j, words 2,3 -> block 2j+1; fold e4m3 into f16
+    // words 0,1 -> block 2j, words 2,3 -> block 2j+1; fold e4m3 into f16.
+    // Zero, subnormal or NaN scale codes anywhere in the warp's chunk send
+    // the whole warp through the exact decoder (one uniform branch).
     uint32_t sw[R][2][2];
+    bool slow = false;
 #pragma unroll
     for (int r = 0; r < R; ++r)
 #pragma unroll
-      for (int h = 0; h < 2; ++h)
-        if (!e4m3x2_to_f16x2_fast(cs[r][h], sw[r][h][0], sw[r][h][1])) {
+      for (int h = 0; h < 2; ++h) slow |= !e4m3x2_to_f16x2_fast(cs[r][h], sw[r][h][0], sw[r][h][1]);
+    if (__any_sync(0xFFFFFFFFu, slow)) {
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
           sw[r][h][0] = f16x2_of(e4m3_decode(cs[r][h] & 0xFFu));
           sw[r][h][1] = f16x2_of(e4m3_decode((cs[r][h] >> 8) & 0xFFu));
         }
+    }
 #pragma unroll
     for (int qw = 0; qw < 4; ++qw) {
       uint32_t A[R][2][4];

@@ -1,24 +1,16 @@
-// umma.cu -- tcgen05 (5th-generation tensor core) W4A16 GEMM for larger M.
+// umma.cu -- tile-per-CTA tcgen05 (5th-generation tensor core) W4A16 GEMM
+// for M >= 128 (and for 32 <= M < 128 when K % 256 != 0).
 //
 // Y[M,N] = X[M,K] . W[N,K]^T, W packed in the reference layouts
-// (titoatwork/qgemm-mx include/qgemm/pack.hpp:14-85), X bf16.
+// (titoatwork/qgemm-mx include/qgemm/pack.hpp:14-85); X arrives as the f16
+// copy with per-row power-of-two factors made by k_xprep (gemv.cu).
 //
 // Swap-AB tile: 128 weight rows form the UMMA M side, BN activation rows
 // (32..256) the UMMA N side, so one tcgen05.mma.kind::f16 instruction computes
 // a [128 x BN x 16] slab and the FP32 accumulator D = Y^T tile lives in TMEM
-// (128 lanes x BN columns).  Per K step of 64:
-//   warp 0  (TMA)      cp.async.bulk.tensor loads of the packed W tile
-//                      (128 rows x 32 bytes) and of the X tile (BN rows x 64
-//                      bf16, 128-byte swizzle) into stage s; no multicast.
-//   warps 2..5 (128 threads, one weight row each) dequantise their row's 64
-//                      codes exactly to bf16 (MXFP4: e2m1 * 2^(e8m0-127) and
-//                      NVFP4: e2m1 * e4m3 both fit bf16) and store them in the
-//                      canonical K-major SWIZZLE_128B layout, then fence the
-//                      generic->async proxy and arrive on a_ready[s].
-//   warp 1, lane 0     issues 4 tcgen05.mma (K=16 each) on stage s and
-//                      tcgen05.commit's the stage back to the producer.
-// After the last K step the dequant warps drain TMEM with tcgen05.ld,
-// apply the NVFP4 tensor scale and store bf16/fp32 Y.
+// (128 lanes x BN columns).  The dequantised operand is written straight into
+// TMEM (TS form, below); K is split across CTAs when the tile count alone
+// does not fill the SMs, with a deterministic last-arriver reduction.
 //
 // Every mbarrier wait is bounded by %globaltimer; on timeout the kernel sets
 // g_umma_fault, gives its in-flight copies a bounded chance to land, frees its
@@ -36,7 +28,6 @@ __device__ unsigned g_umma_fault = 0;
 
 constexpr int kUBM = 128;  // weight rows per tile (UMMA M)
 constexpr int kUBK = 64;   // K per stage (one 128-byte swizzle row of bf16)
-constexpr int kUThreads = 192;
 
 struct UmmaArgs {
   const void* scales;
@@ -56,236 +47,6 @@ struct UmmaArgs {
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
   return mbar_wait_flag(bar, parity, &g_umma_fault);
 }
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }"
-      ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(acc)
-      : "memory");
-}
-
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t s) {
-  uint32_t d;
-  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(s));
-  return d;
-}
-__device__ __forceinline__ uint32_t hmul2_bf16(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-
-// 8 E2M1 codes (nibble i = k offset i) -> bf16x2 words (c0,c1)(c2,c3)(c4,c5)
-// (c6,c7): byte-permute lookups of the bf16 bytes of {0,.5,1,1.5,2,3,4,6};
-// the sign bit of each code is replicated into its high byte.
-__device__ __forceinline__ void e2m1x8_to_bf16(uint32_t q, uint32_t (&o)[4]) {
-  constexpr uint32_t LO_A = 0xC0800000u, LO_B = 0xC0804000u;
-  constexpr uint32_t HI_A = 0x3F3F3F00u, HI_B = 0x40404040u;
-  const uint32_t s0 = q & 0x7777u, s1 = (q >> 16) & 0x7777u;
-  const uint32_t lo0 = prmt(LO_A, LO_B, s0), lo1 = prmt(LO_A, LO_B, s1);
-  uint32_t hi0 = prmt(HI_A, HI_B, s0), hi1 = prmt(HI_A, HI_B, s1);
-  const uint32_t q4 = q << 4;
-  hi0 |= prmt(q4, q, 0xD9C8u) & 0x80808080u;
-  hi1 |= prmt(q4, q, 0xFBEAu) & 0x80808080u;
-  o[0] = prmt(lo0, hi0, 0x5140u);
-  o[1] = prmt(lo0, hi0, 0x7362u);
-  o[2] = prmt(lo1, hi1, 0x5140u);
-  o[3] = prmt(lo1, hi1, 0x7362u);
-}
-
-// bf16x2 multiplier for a block scale, and whether the scaled values are
-// exact with one bf16 multiply (normal bf16 results).
-__device__ __forceinline__ uint32_t mx_scale_bf16(uint32_t sb, bool& slow) {
-  sb &= 0xFFu;
-  slow = sb <= 1u;  // products can be subnormal: computed in fp32 instead
-  const uint32_t b = (sb == 0xFFu) ? 0x7FC0u : (sb << 7);
-  return b | (b << 16);
-}
-__device__ __forceinline__ uint32_t nv_scale_bf16(uint32_t sb) {
-  const uint32_t b = f2u(e4m3_decode(sb & 0xFFu)) >> 16;  // exact (4 significant bits)
-  return b | (b << 16);
-}
-
-// ---------------------------------------------------------------------------
-// Kernel
-// ---------------------------------------------------------------------------
-
-template <int BN, int STAGES>
-struct USmem {
-  static constexpr int A_BYTES = kUBM * kUBK * 2;   // 16 KB dequantised W (bf16)
-  static constexpr int B_BYTES = BN * kUBK * 2;     // X tile (bf16)
-  static constexpr int P_BYTES = kUBM * kUBK / 2;   // packed W (4 KB)
-  static constexpr int STAGE = A_BYTES + B_BYTES + P_BYTES;
-  static constexpr int BYTES = STAGES * STAGE + 1024 /*align*/ + 256 /*barriers*/;
-};
-
-template <int FMT, int BN, int STAGES, bool F32OUT>
-__global__ void __launch_bounds__(kUThreads, 1)
-k_umma(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x, const UmmaArgs a) {
-  using L = USmem<BN, STAGES>;
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t raw = su32(smem_raw);
-  const uint32_t base = (raw + 1023u) & ~1023u;  // SWIZZLE_128B tiles want 1024-byte alignment
-  uint8_t* gbase = smem_raw + (base - raw);
-  // stage s: [A | B | P]
-  auto A_addr = [&](int s) { return base + (uint32_t)(s * L::STAGE); };
-  auto B_addr = [&](int s) { return base + (uint32_t)(s * L::STAGE + L::A_BYTES); };
-  auto P_ptr = [&](int s) { return gbase + s * L::STAGE + L::A_BYTES + L::B_BYTES; };
-  uint64_t* bars = reinterpret_cast<uint64_t*>(gbase + STAGES * L::STAGE);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 1);
-  auto full_bar = [&](int s) { return su32(&bars[s]); };
-  auto aready_bar = [&](int s) { return su32(&bars[STAGES + s]); };
-  auto empty_bar = [&](int s) { return su32(&bars[2 * STAGES + s]); };
-  const uint32_t acc_bar = su32(&bars[3 * STAGES]);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * kUBM, m0 = blockIdx.y * BN;
-  const int ksteps = a.K / kUBK;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(full_bar(s), 1);
-      mbar_init(aready_bar(s), 128);
-      mbar_init(empty_bar(s), 1);
-    }
-    mbar_init(acc_bar, 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  if (warp == 1) {  // TMEM: BN fp32 columns x 128 lanes
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_slot)),
-                 "r"((uint32_t)BN));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  bool ok = true;
-
-  if (warp == 0) {
-    // ---------------- producer ----------------
-    if (lane == 0) {
-      const uint32_t tx = (uint32_t)(L::B_BYTES + L::P_BYTES);
-      for (int ks = 0; ks < ksteps && ok; ++ks) {
-        const int s = ks % STAGES;
-        if (ks >= STAGES) ok = mbar_wait(empty_bar(s), ((ks / STAGES) + 1) & 1);
-        if (!ok) break;
-        mbar_expect_tx(full_bar(s), tx);
-        tma_load_2d(B_addr(s), &map_x, ks * kUBK, m0, full_bar(s));
-        tma_load_2d(su32(P_ptr(s)), &map_w, ks * (kUBK / 2), n0, full_bar(s));
-      }
-    }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16(kUBM, BN);
-      for (int ks = 0; ks < ksteps && ok; ++ks) {
-        const int s = ks % STAGES;
-        ok = mbar_wait(aready_bar(s), (ks / STAGES) & 1);
-        if (!ok) break;
-        tc_fence_after();
-        const uint64_t ad = sw128_desc(A_addr(s)), bd = sw128_desc(B_addr(s));
-#pragma unroll
-        for (int kk = 0; kk < kUBK / 16; ++kk)  // +32 bytes along K per MMA
-          umma_bf16(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (ks | kk) != 0);
-        umma_commit(empty_bar(s));
-      }
-      umma_commit(acc_bar);
-    }
-  } else {
-    // ---------------- dequant (128 threads, one weight row each) ----------------
-    const int r = threadIdx.x - 64;  // 0..127
-    const int n = n0 + r;
-    const bool live = n < a.N;
-    const uint8_t* sc8 = static_cast<const uint8_t*>(a.scales);
-    auto load_scale = [&](int ks) -> uint32_t {
-      if (!live) return 0u;
-      if (FMT == 0) return *reinterpret_cast<const uint16_t*>(sc8 + (size_t)n * (a.K / 32) + ks * 2);
-      return *reinterpret_cast<const uint32_t*>(sc8 + (size_t)n * (a.K / 16) + ks * 4);
-    };
-    uint32_t scn = load_scale(0);
-    // A tile row r: atom r/8, row r%8 inside the atom; 16-byte chunk c at (c ^ r%8)
-    const uint32_t row_off = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
-    for (int ks = 0; ks < ksteps && ok; ++ks) {
-      const int s = ks % STAGES;
-      const uint32_t sc = scn;
-      if (ks + 1 < ksteps) scn = load_scale(ks + 1);
-      ok = mbar_wait(full_bar(s), (ks / STAGES) & 1);
-      if (!ok) break;
-      const uint4* prow = reinterpret_cast<const uint4*>(P_ptr(s) + r * 32);
-      const uint4 p0 = prow[0], p1 = prow[1];
-      const uint32_t q[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-      uint8_t* arow = gbase + (A_addr(s) - base) + row_off;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {  // chunk c = codes 8c..8c+7
-        uint32_t o[4];
-        e2m1x8_to_bf16(q[c], o);
-        if (FMT == 0) {
-          bool slow;
-          const uint32_t m2 = mx_scale_bf16(sc >> (8 * (c >> 2)), slow);
-          if (slow) {
-            const float f = e8m0_decode(sc >> (8 * (c >> 2)));
-#pragma unroll
-            for (int p = 0; p < 4; ++p) {
-              const float f0 = e2m1_decode(q[c] >> (8 * p)) * f, f1 = e2m1_decode(q[c] >> (8 * p + 4)) * f;
-              o[p] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(f0)) |
-                     ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(f1)) << 16);
-            }
-          } else {
-#pragma unroll
-            for (int p = 0; p < 4; ++p) o[p] = hmul2_bf16(o[p], m2);
-          }
-        } else {
-          const uint32_t m2 = nv_scale_bf16(sc >> (8 * (c >> 1)));
-#pragma unroll
-          for (int p = 0; p < 4; ++p) o[p] = hmul2_bf16(o[p], m2);
-        }
-        *reinterpret_cast<uint4*>(arow + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
-      }
-      fence_proxy_async();  // generic-proxy smem writes -> visible to tcgen05.mma
-      mbar_arrive(aready_bar(s));
-    }
-
-    // ---------------- epilogue ----------------
-    if (ok) ok = mbar_wait(acc_bar, 0);
-    tc_fence_after();
-    if (ok) {
-      const int q = warp & 3;              // TMEM lane quadrant this warp may access
-      const int row = 32 * q + lane;       // D row = weight row
-      const int nn = n0 + row;
-      const float post = (FMT == 1) ? a.ts : 1.0f;
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        uint32_t v[16];
-        tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
-        if (nn < a.N) {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int m = m0 + c0 + i;
-            if (m < a.M) {
-              const float y = u2f(v[i]) * post;
-              if (F32OUT) static_cast<float*>(a.Y)[(size_t)m * a.N + nn] = y;
-              else static_cast<__nv_bfloat16*>(a.Y)[(size_t)m * a.N + nn] = __float2bfloat16_rn(y);
-            }
-          }
-        }
-      }
-    }
-  }
-
-  if (!ok && threadIdx.x == 0) {
-    // give copies / MMAs still in flight a bounded chance to land
-    for (int s = 0; s < STAGES; ++s) { (void)mbar_try(full_bar(s), 0); }
-    const unsigned long long t0 = gtimer();
-    while (gtimer() - t0 < 50000000ull) { }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)BN));
-  }
-}
-
 // ---------------------------------------------------------------------------
 // TS variant: dequantised W in TMEM, f16 operands
 // ---------------------------------------------------------------------------
@@ -578,34 +339,6 @@ bool make_tma_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr, 
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int FMT, int BN, int STAGES, bool F32>
-static cudaError_t launch_umma_t(const CUtensorMap& mw, const CUtensorMap& mx, const UmmaArgs& a, cudaStream_t s) {
-  using L = USmem<BN, STAGES>;
-  static bool attr[64] = {false};
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  if (dev >= 0 && dev < 64 && !attr[dev]) {
-    e = cudaFuncSetAttribute(k_umma<FMT, BN, STAGES, F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
-    if (e != cudaSuccess) return e;
-    attr[dev] = true;
-  }
-  dim3 grid((unsigned)((a.N + kUBM - 1) / kUBM), (unsigned)((a.M + BN - 1) / BN));
-  k_umma<FMT, BN, STAGES, F32><<<grid, kUThreads, L::BYTES, s>>>(mw, mx, a);
-  return cudaGetLastError();
-}
-
-template <int FMT, bool F32>
-static cudaError_t launch_umma_bn(int bn, const CUtensorMap& mw, const CUtensorMap& mx, const UmmaArgs& a,
-                                  cudaStream_t s) {
-  switch (bn) {
-    case 32: return launch_umma_t<FMT, 32, 8, F32>(mw, mx, a, s);
-    case 64: return launch_umma_t<FMT, 64, 6, F32>(mw, mx, a, s);
-    case 128: return launch_umma_t<FMT, 128, 5, F32>(mw, mx, a, s);
-    default: return launch_umma_t<FMT, 256, 4, F32>(mw, mx, a, s);
-  }
-}
-
 // Largest supported tile width not above M, so a TMA box never exceeds the
 // X tensor's row count.
 template <int FMT, int BN, int STAGES, bool F32>
@@ -646,29 +379,6 @@ static cudaError_t launch_ts_bn(int bn, const CUtensorMap& mw, const CUtensorMap
 }
 
 int umma_bn_for(int M) { return M >= 256 ? 256 : M >= 128 ? 128 : M >= 64 ? 64 : 32; }
-
-// Supported: MXFP4 / NVFP4, K % 64 == 0.  Returns QGEMM_ERR_UNSUPPORTED_SHAPE otherwise.
-qgemm_status_t gemm_umma(const qgemm_weights_t* w, const uint16_t* X, int M, void* Y, bool f32, cudaStream_t s) {
-  if (w->format != QGEMM_FMT_MXFP4 && w->format != QGEMM_FMT_NVFP4)
-    return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "umma path: MXFP4 / NVFP4 only");
-  if (w->K % kUBK != 0 || w->K > (size_t)INT32_MAX || w->N > (size_t)INT32_MAX)
-    return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "umma path: K must be a multiple of %d", kUBK);
-  const int bn = umma_bn_for(M);
-  CUtensorMap mw, mx;
-  if (!make_tma_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->data, w->K / 2, w->N, w->K / 2, kUBK / 2, kUBM,
-                   CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !make_tma_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, X, w->K, (uint64_t)M, w->K * 2, kUBK, (uint32_t)bn,
-                   CU_TENSOR_MAP_SWIZZLE_128B))
-    return fail(QGEMM_ERR_CUDA, "umma path: cuTensorMapEncodeTiled failed");
-  UmmaArgs a;
-  a.scales = w->scales; a.Y = Y; a.M = M; a.N = (int)w->N; a.K = (int)w->K; a.ts = w->tensor_scale;
-  a.splits = 1; a.partials = nullptr; a.counters = nullptr;
-  cudaError_t e;
-  if (w->format == QGEMM_FMT_MXFP4) e = f32 ? launch_umma_bn<0, true>(bn, mw, mx, a, s) : launch_umma_bn<0, false>(bn, mw, mx, a, s);
-  else e = f32 ? launch_umma_bn<1, true>(bn, mw, mx, a, s) : launch_umma_bn<1, false>(bn, mw, mx, a, s);
-  if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "umma launch: %s", cudaGetErrorString(e));
-  return QGEMM_OK;
-}
 
 // TS path: Xh / xs are the f16 copy of X and its row factors (k_xprep).
 // K splits for a launch: enough CTAs to fill every SM slot when the tile
