@@ -143,15 +143,17 @@ qgemm_status_t qgemm_gemm_w4a16_f32(const qgemm_weights_t* w, const uint16_t* X,
  * gather of Y are the multi-GPU step its bench is extended with.
  * qgemm_tp_gemm_w4a16 computes this rank's Y slice with qgemm_gemm_w4a16's
  * kernels, writes it into every rank's Y_full [M][N] through peer pointers
- * (y_peers[d] = rank d's Y_full as mapped in this process), then announces
- * the call in every rank's sync block and waits (bounded, 2 s) until all
- * ranks' slices have landed in its own Y_full.  Every rank makes the same
+ * (y_peers[d] = rank d's Y_full as mapped in this process), adds its
+ * arrival to every rank's sync block (system-scope release after the
+ * stores) and waits (bounded, 2 s) until every rank's arrival for this call
+ * has reached its own sync block, i.e. all slices have landed in its own
+ * Y_full.  Every rank makes the same
  * sequence of calls; a rank's Y_full is written by all ranks, so reuse a
  * buffer only once every rank is done reading the previous result.
  * sync_peers[d]: rank d's sync block, qgemm_tp_sync_bytes() bytes, zeroed
  * once.  workspace: qgemm_tp_workspace_size(w_local, M) bytes, zeroed once
- * (qgemm_workspace_init).  Graph-capturable: the call's sequence number is
- * a device-side counter in the sync block. */
+ * (qgemm_workspace_init).  Graph-capturable: the arrival and expected
+ * counts are device-side counters in the sync block. */
 size_t qgemm_tp_sync_bytes(int32_t world);
 size_t qgemm_tp_workspace_size(const qgemm_weights_t* w_local, int32_t M);
 qgemm_status_t qgemm_tp_gemm_w4a16(const qgemm_weights_t* w_local, const uint16_t* X,

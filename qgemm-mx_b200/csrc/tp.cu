@@ -1,24 +1,22 @@
 // tp.cu -- tensor-parallel W4A16 GEMM over the GPUs of one node, W sharded
 // along N, with the all-gather of Y done over NVLink peer memory.
 //
-// Rank r holds rows [r N/world, (r+1) N/world) of W.  One call:
-//   1. the local GEMM (qgemm_gemm_w4a16's dispatch) writes Y's slice into a
-//      local staging buffer in the workspace;
-//   2. k_tp_gather copies the slice into every rank's Y_full [M][N] at
-//      columns [r N/world, (r+1) N/world) with plain stores through the
-//      peer mappings (NVLink P2P; no library collective, no TMA); its last
-//      CTA makes the stores visible system-wide, raises this call's epoch
-//      in every rank's sync block and waits until every rank's epoch for
-//      this call has arrived in its own block.
-// The epoch is a device-side counter in the sync block, so the launches can
-// be captured in a CUDA graph and replayed.  The wait is
-// bounded (2 s); on timeout the kernel records it and qgemm_tp_status
-// reports QGEMM_ERR_TIMEOUT.  Every rank must make the same sequence of
-// calls.
+// Rank r holds rows [r N/world, (r+1) N/world) of W.  The TMA decode and
+// stream-K tcgen05 kernels store their bf16 results straight into every
+// rank's Y_full [M][N] at columns [r N/world, (r+1) N/world) through the peer
+// mappings (NVLink P2P stores) and finish with the arrival exchange of
+// tp.cuh.  The other kernels write the slice into a staging buffer in the
+// workspace, and k_tp_gather copies it to every rank and does the same
+// exchange.  No library collective, no TMA on peer memory.
+//
+// The counts live in device memory, so the launches can be captured in a
+// CUDA graph and replayed.  The wait is bounded (2 s); on timeout the kernel
+// records it and qgemm_tp_status reports QGEMM_ERR_TIMEOUT.  Every rank must
+// make the same sequence of calls.
 //
 // Sync block of a rank (qgemm_tp_sync_bytes): uint32 [kTpMaxWorld] arrival
-// slots (slot s = latest epoch rank s announced to this rank), the local
-// call counter and the CTA ticket counter; zero it once before first use.
+// slots (slot s counts what rank s has delivered to this rank), the expected
+// count and a reserved word; zero it once before first use.
 #include <cuda.h>
 #include <cuda_bf16.h>
 

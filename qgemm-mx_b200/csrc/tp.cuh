@@ -3,13 +3,24 @@
 //
 // A kernel given a TpOut with world > 0 stores each bf16 result at
 // y[d][m * ldy + col0 + n] for every rank d (the peer mappings; NVLink P2P
-// stores), and finishes with tp_finish: every thread fences its stores at
-// system scope, the CTA takes a ticket, and the CTA that finishes last
-// announces the call's epoch in every rank's sync block and waits (bounded)
-// until every rank has announced it in this rank's block.
+// stores) and ends with tp_finish, called by every thread of every CTA:
+//   * after a CTA barrier, one thread per destination rank d adds the CTA's
+//     share to arrival slot [rank] of rank d's sync block with a
+//     system-scope release reduction.  The release is cumulative over the
+//     whole CTA's stores (they precede it through the barrier), so a rank
+//     that has seen a sender's shares has seen the stores behind them.
+//     The shares of a call's CTAs sum to exactly kTpCallUnits whatever the
+//     grid size: share(b) = floor((b + 1) U / G) - floor(b U / G);
+//   * CTA 0 raises this rank's expected count by kTpCallUnits and waits
+//     (bounded, acquire loads of its own sync block) until every rank's slot
+//     has reached it.
+// Counters wrap modulo 2^32 and are compared by signed difference, which is
+// exact while ranks are fewer than 2^15 calls apart (a rank is at most one
+// call ahead: it waits for the others at the end of every call).
 //
-// Sync block of a rank: uint32 [kTpMaxWorld] arrival slots, the local call
-// counter, the CTA ticket counter (qgemm_tp_sync_bytes).
+// Sync block of a rank (uint32 words, qgemm_tp_sync_bytes): [0, kTpMaxWorld)
+// arrival slots, then the expected count, then one reserved word.  Zero it
+// once before the first call; every rank must make the same sequence of calls.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -20,6 +31,7 @@ namespace qg {
 
 constexpr int kTpMaxWorld = 8;
 constexpr unsigned long long kTpWaitNs = 2000000000ull;  // 2 s
+constexpr uint32_t kTpCallUnits = 1u << 16;              // arrival units per call and sender
 
 struct TpOut {
   int world;   // 0: not a tensor-parallel launch
@@ -45,34 +57,29 @@ __device__ __forceinline__ unsigned long long tp_gtimer() {
 // Called by every thread of every CTA after its last Y store; a wait that
 // gives up sets *fault (the calling kernel's own flag).
 __device__ __forceinline__ void tp_finish(const TpOut& t, unsigned* fault) {
-  __threadfence_system();  // this thread's peer stores are performed
-  __syncthreads();
-  uint32_t* mine = t.sync[t.rank];
-  __shared__ unsigned s_tp_last;
-  __shared__ uint32_t s_tp_epoch;
-  if (threadIdx.x == 0) s_tp_last = (atomicAdd(mine + kTpMaxWorld + 1, 1u) == gridDim.x - 1) ? 1u : 0u;
-  __syncthreads();
-  if (!s_tp_last || threadIdx.x >= 32) return;
-  // the last CTA: every CTA's stores were fenced before its ticket
-  const int lane = threadIdx.x;
-  if (lane == 0) {
-    mine[kTpMaxWorld + 1] = 0u;                 // ticket counter back to zero for the next launch
-    const uint32_t e = mine[kTpMaxWorld] + 1u;  // call counter: same sequence on every rank
-    mine[kTpMaxWorld] = e;
-    s_tp_epoch = e;
+  __syncthreads();  // every store of this CTA precedes the releases below
+  const int tid = threadIdx.x;
+  if (tid < t.world) {
+    const uint32_t G = gridDim.x, b = blockIdx.x;
+    const uint32_t share = (uint32_t)((((unsigned long long)(b + 1)) * kTpCallUnits) / G -
+                                      (((unsigned long long)b) * kTpCallUnits) / G);
+    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(t.sync[tid] + t.rank), "r"(share) : "memory");
   }
-  __syncwarp();
-  const uint32_t epoch = s_tp_epoch;
-  asm volatile("fence.acq_rel.sys;" ::: "memory");
-  if (lane < t.world)
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(t.sync[lane] + t.rank), "r"(epoch) : "memory");
+  if (blockIdx.x != 0 || tid >= 32) return;
+  uint32_t* mine = t.sync[t.rank];
+  uint32_t expect = 0;
+  if (tid == 0) {  // only CTA 0 of this rank's launches touches the expected count; launches are stream-ordered
+    expect = mine[kTpMaxWorld] + kTpCallUnits;
+    mine[kTpMaxWorld] = expect;
+  }
+  expect = __shfl_sync(0xFFFFFFFFu, expect, 0);
   bool ok = true;
-  if (lane < t.world) {
+  if (tid < t.world) {
     const unsigned long long t0 = tp_gtimer();
     for (;;) {
       uint32_t v;
-      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine + lane) : "memory");
-      if ((int32_t)(v - epoch) >= 0) break;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine + tid) : "memory");
+      if ((int32_t)(v - expect) >= 0) break;
       if (tp_gtimer() - t0 > kTpWaitNs) { ok = false; break; }
     }
   }
