@@ -88,9 +88,10 @@ struct GemvArgs {
 //     and each 64-k block, BN rows of 128 bytes whose 16-byte chunk c is
 //     stored at chunk c ^ (row % 8) -- the shared-memory image of a
 //     128-byte-swizzled K-major tile, so one linear bulk copy stages it.
-//  2  TMA decode image (lp = mpad rows): for each 256-k unit, mpad rows of 32
-//     16-byte chunks, chunk c of row m at (c & ~7) | ((c ^ m) & 7), so the
-//     warp-MMA fragment loads from shared memory are free of bank conflicts.
+//  2, 3  TMA decode image (lp = mpad rows): for each 256-k unit, mpad rows
+//     of 32 16-byte chunks, chunk c of row m at xg_pos(c, m) (gemv_core.cuh;
+//     2 for MXFP4 and 3 for NVFP4 consumers), so the warp-MMA fragment loads
+//     from shared memory are free of bank conflicts.
 // Rows M .. (padded row count) - 1 (one CTA each) are written as zeros.
 __device__ __forceinline__ size_t xprep_index(int m, int k, int K, int layout, int lp) {
   if (layout == 0) return (size_t)m * K + k;
@@ -99,8 +100,7 @@ __device__ __forceinline__ size_t xprep_index(int m, int k, int K, int layout, i
     return (((size_t)mb * (K >> 6) + kb) * lp + r) * 64 + (size_t)((c ^ (r & 7)) << 3);
   }
   const int u = k >> 8, c = (k >> 3) & 31;
-  const int pos = (c & ~7) | ((c ^ m) & 7);
-  return (((size_t)u * lp + m) * 32 + pos) * 8;
+  return (((size_t)u * lp + m) * 32 + xg_pos(layout == 2 ? 0 : 1, c, m)) * 8;
 }
 // One pass: every thread issues all its 16-byte loads of the row before it
 // uses any (up to kXpChunks of them, i.e. K <= 256 * 8 * kXpChunks), keeps
@@ -621,7 +621,8 @@ qgemm_status_t gemm_decode_ex(const qgemm_weights_t* w, const uint16_t* X, int M
     for (int m0 = 0; m0 < M; m0 += kMaxM) {
       const int mb = (M - m0) < kMaxM ? (M - m0) : kMaxM;
       const int mpad = mb <= 8 ? 8 : 16;
-      QG_CUDA_RET(launch_xprep(X + (size_t)m0 * w->K, mb, mpad, (int)w->K, 0, 2, mpad, xg, xs, s));
+      QG_CUDA_RET(launch_xprep(X + (size_t)m0 * w->K, mb, mpad, (int)w->K, 0,
+                               w->format == QGEMM_FMT_NVFP4 ? 3 : 2, mpad, xg, xs, s));
       if (tp) {  // this block's rows of every rank's Y_full
         TpOut tb = *tp;
         for (int d = 0; d < tb.world; ++d) tb.y[d] += (size_t)m0 * tb.ldy;

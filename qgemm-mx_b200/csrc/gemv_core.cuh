@@ -12,6 +12,15 @@
 
 namespace qg {
 
+// Position of 8-f16 chunk idx of X row m in the staged X tile (the image
+// k_xprep writes, layout 2 for MXFP4 and 3 for NVFP4): a per-row permutation within each aligned
+// group of 8 chunks chosen so that the consumers' 128-bit fragment loads
+// (two rows and four lanes per phase) hit eight distinct bank groups.
+__host__ __device__ __forceinline__ int xg_pos(int fmt, int idx, int m) {
+  const int f = fmt == 0 ? ((m & 1) << 2) : ((((idx >> 3) & 1) << 1) ^ (m & 1));
+  return (idx & ~7) | ((idx ^ f) & 7);
+}
+
 // ---------------------------------------------------------------------------
 // small PTX helpers
 // ---------------------------------------------------------------------------

@@ -14,19 +14,20 @@
 // tiles split across CTAs are reduced through the workspace by the CTA whose
 // ticket shows it arrived last, summing contributors in CTA order.
 //
-// Warp roles (576 or 320 threads):
+// Warp roles (448 or 320 threads):
 //   warps 0, 1   producers, alternate units.  Lane 0 arms the stage's
 //                mbarrier and issues the packed-W box (TMA, 128 rows x 128 B,
 //                128-byte swizzle) and the unit's X tile (one linear bulk copy
-//                of the image k_xprep wrote, layout 2); all 32 lanes copy the
-//                unit's scale bytes with 4-byte cp.async and arrive on the
+//                of the image k_xprep wrote, layout 2 / 3); all 32 lanes copy
+//                the unit's scale bytes with 4-byte cp.async and arrive on the
 //                same mbarrier when their copies land.  No multicast.
-//   warps 2..    consumers.  M <= 8: sixteen warps, warp (g, c) owns weight
-//                rows 16g .. 16g + 15 and 128-k chunk c of every unit; the
-//                pair's sums are added (chunk 0 + chunk 1) at each segment
-//                end.  M <= 16: eight warps, one per 16-row group, both chunks.
-//                Each runs chunk_mma on codes, scales and X fragments read
-//                from the stage.
+//   warps 2..    consumers, in unit groups (GtCfg): unit i of the CTA's range
+//                goes to group i % UG, whose warps each own 16 RPW weight rows
+//                and all 256 k of it and run chunk_mma on codes, scales and X
+//                fragments read from the stage.  M <= 8: three groups of four
+//                warps (32 rows each); M <= 16: one group of eight (16 rows).
+//                At each segment end the groups' sums are added in group
+//                order and group 0 stores the tile or its stream-K partial.
 // Every mbarrier wait is bounded (tc.cuh); on timeout the kernel sets
 // g_gemv_tma_fault and returns after letting copies in flight land.
 #include <cuda.h>
@@ -46,12 +47,15 @@ constexpr int kGtRows = 128;
 constexpr int kGtProd = 2;
 constexpr int kGtGroups = 8;   // 16-row groups per 128-row tile
 
-template <int FMT, int NT>
+// Consumer layout: UG unit groups of WPG = 8 / RPW warps.  Unit i of a
+// CTA's range goes to group i % UG; within the group, warp w owns weight rows
+// [16 RPW w, 16 RPW (w + 1)) of the unit and all of its 256 k (RPW 16-row MMA
+// tiles, so every X fragment read from shared memory feeds RPW MMAs).  At the
+// end of each tile segment the groups' sums are added in group order.
+template <int FMT, int NT, int RPW, int UG>
 struct GtCfg {
-  // consumers: one warp per (16-row group, 128-k chunk) when registers allow
-  // (NT = 1), else one warp per 16-row group covering both chunks
-  static constexpr int KSPLIT = NT == 1 ? 2 : 1;
-  static constexpr int CONS = kGtGroups * KSPLIT;
+  static constexpr int WPG = kGtGroups / RPW;                          // warps per unit group
+  static constexpr int CONS = WPG * UG;
   static constexpr int THREADS = 32 * (kGtProd + CONS);
   static constexpr int MPAD = 8 * NT;
   static constexpr int SB = (FMT == 0) ? kGtUnitK / 32 : kGtUnitK / 16;   // scale bytes per row per unit
@@ -59,8 +63,9 @@ struct GtCfg {
   static constexpr int X_BYTES = MPAD * kGtUnitK * 2;
   static constexpr int S_BYTES = kGtRows * SB;
   static constexpr int STAGE = ((W_BYTES + X_BYTES + S_BYTES) + 1023) / 1024 * 1024;
-  static constexpr int STAGES = ((200 * 1024) / STAGE) & ~1;            // even: two producers
-  static constexpr int BYTES = 1024 + STAGES * STAGE + 2 * STAGES * 8 + 16 + (KSPLIT - 1) * kGtGroups * NT * 32 * 16;
+  static constexpr int PART_BYTES = (UG - 1) * kGtGroups * NT * 32 * 16;  // other groups' sums
+  static constexpr int STAGES = ((200 * 1024 - PART_BYTES) / STAGE) & ~1;  // even: two producers
+  static constexpr int BYTES = 1024 + STAGES * STAGE + 2 * STAGES * 8 + 16 + PART_BYTES;
   static_assert(BYTES <= 232448, "shared memory");
   static_assert(STAGES >= 4, "ring depth");
 };
@@ -80,10 +85,10 @@ struct GtArgs {
   TpOut tp;              // world > 0: store into every rank's Y_full, then tp_finish
 };
 
-template <int FMT, int NT, bool F32OUT>
-__global__ void __launch_bounds__(GtCfg<FMT, NT>::THREADS, 1)
+template <int FMT, int NT, int RPW, int UG, bool F32OUT>
+__global__ void __launch_bounds__(GtCfg<FMT, NT, RPW, UG>::THREADS, 1)
 k_gemv_tma(const __grid_constant__ CUtensorMap map_w, const GtArgs a) {
-  using C = GtCfg<FMT, NT>;
+  using C = GtCfg<FMT, NT, RPW, UG>;
   constexpr int kGtCons = C::CONS;
   constexpr int S = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -98,7 +103,7 @@ k_gemv_tma(const __grid_constant__ CUtensorMap map_w, const GtArgs a) {
   auto full_bar = [&](int s) { return su32(&bars[s]); };
   auto empty_bar = [&](int s) { return su32(&bars[S + s]); };
   unsigned* s_ticket = reinterpret_cast<unsigned*>(bars + 2 * S);
-  float4* s_half = reinterpret_cast<float4*>(bars + 2 * S + 2);  // [8 groups][NT][32]: chunk-1 sums
+  float4* s_part = reinterpret_cast<float4*>(bars + 2 * S + 2);  // [UG - 1][8 row groups][NT][32]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long it0 = (long long)blockIdx.x * a.T / a.G;
@@ -110,7 +115,7 @@ k_gemv_tma(const __grid_constant__ CUtensorMap map_w, const GtArgs a) {
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(full_bar(s), 1 + 32);   // lane 0's expect_tx arrival + 32 cp.async arrivals
-      mbar_init(empty_bar(s), kGtCons);
+      mbar_init(empty_bar(s), C::WPG);  // the unit's group
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -121,211 +126,218 @@ k_gemv_tma(const __grid_constant__ CUtensorMap map_w, const GtArgs a) {
     // ------------------------------ producers ---------------------------------
     const int p = warp;
     const size_t srow = (size_t)a.K / (FMT == 0 ? 32 : 16);
-    auto issue_wx = [&](int i, bool with_w, bool with_x) {
-      const int s = i % S;
-      const long long it = it0 + i;
-      const int tile = (int)(it / KS), ks = (int)(it % KS);
-      if (with_w) {
-        mbar_expect_tx(full_bar(s), (uint32_t)(C::W_BYTES + C::X_BYTES));
-        tma_load_2d(base + (uint32_t)W_off(s), &map_w, ks * (kGtUnitK / 2), tile * kGtRows, full_bar(s));
-      }
-      if (with_x) {
-        const uint8_t* src = a.xg + (size_t)ks * C::X_BYTES;
-        asm volatile(
-            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-            ::"r"(base + (uint32_t)X_off(s)), "l"(src), "r"((uint32_t)C::X_BYTES), "r"(full_bar(s))
-            : "memory");
-      }
+    // (tile, k-unit) of this producer's next unit, advanced by kGtProd units
+    // per issue: no 64-bit division in the loop.
+    int p_tile = (int)((it0 + p) / KS), p_ks = (int)((it0 + p) % KS);
+    auto advance = [&]() {
+      p_ks += kGtProd;
+      while (p_ks >= KS) { p_ks -= KS; ++p_tile; }
     };
-    auto issue_scales = [&](int i) {
-      const int s = i % S;
-      const long long it = it0 + i;
-      const int tile = (int)(it / KS), ks = (int)(it % KS);
+    auto issue_w = [&](int s) {
+      mbar_expect_tx(full_bar(s), (uint32_t)(C::W_BYTES + C::X_BYTES));
+      tma_load_2d(base + (uint32_t)W_off(s), &map_w, p_ks * (kGtUnitK / 2), p_tile * kGtRows, full_bar(s));
+    };
+    auto issue_x = [&](int s, int ks) {
+      const uint8_t* src = a.xg + (size_t)ks * C::X_BYTES;
+      asm volatile(
+          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+          ::"r"(base + (uint32_t)X_off(s)), "l"(src), "r"((uint32_t)C::X_BYTES), "r"(full_bar(s))
+          : "memory");
+    };
+    auto issue_scales = [&](int s) {
       constexpr int WPR = C::SB / 4;  // 4-byte words per row
 #pragma unroll
       for (int e = lane; e < kGtRows * WPR; e += 32) {
         const int row = e / WPR, wi = e % WPR;
-        int n = tile * kGtRows + row;
+        int n = p_tile * kGtRows + row;
         n = n < a.N ? n : a.N - 1;  // rows past N: TMA zero-fills their codes
-        const uint8_t* src = a.scales + (size_t)n * srow + (size_t)ks * C::SB + 4 * wi;
+        const uint8_t* src = a.scales + (size_t)n * srow + (size_t)p_ks * C::SB + 4 * wi;
         asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(base + (uint32_t)(S_off(s) + row * C::SB + 4 * wi)),
                      "l"(src) : "memory");
       }
       asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(full_bar(s)) : "memory");
     };
     const int pre = niter < S ? niter : S;
-    // Weights and scales do not depend on the X-preparation grid: start them first.
+    // Weights and scales do not depend on the X-preparation grid: start them
+    // first; the first stages' X copies follow once that grid is done.
     for (int i = p; i < pre; i += kGtProd) {
-      if (lane == 0) issue_wx(i, true, false);
-      issue_scales(i);
+      if (lane == 0) issue_w(i % S);
+      issue_scales(i % S);
+      advance();
     }
     if (lane == 0) {
       asm volatile("griddepcontrol.wait;" ::: "memory");
-      for (int i = p; i < pre; i += kGtProd) issue_wx(i, false, true);
+      for (int i = p; i < pre; i += kGtProd) issue_x(i % S, (int)((it0 + i) % KS));
     }
     for (int i = pre + ((p - pre % kGtProd + kGtProd) % kGtProd); i < niter; i += kGtProd) {
       const int s = i % S;
       if (lane == 0) ok = mbar_wait_flag(empty_bar(s), ((i / S) + 1) & 1, fault);
       ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
       if (!ok) break;
-      if (lane == 0) issue_wx(i, true, true);
-      issue_scales(i);
+      if (lane == 0) { issue_w(s); issue_x(s, p_ks); }
+      issue_scales(s);
+      advance();
     }
   } else {
     // ------------------------------ consumers ---------------------------------
+    constexpr int WPG = C::WPG;
     const int cons = warp - kGtProd;
-    const int cw_id = cons % kGtGroups;             // weight rows 16 cw_id .. + 15
-    const int kpart = cons / kGtGroups;             // KSPLIT == 2: chunk kpart of each unit
+    const int ug = cons / WPG;                      // unit group: the units i with i % UG == ug
+    const int wq = cons % WPG;                      // weight rows [16 RPW wq, 16 RPW (wq + 1)) of a unit
     const int g = lane >> 2, j = lane & 3;
-    const int row0 = 16 * cw_id + g, row1 = row0 + 8;
-    const uint32_t sw = (uint32_t)(g & 7);         // row0 % 8 == row1 % 8 == g
+    const uint32_t sw = (uint32_t)(g & 7);         // every row this lane touches is g mod 8
     asm volatile("griddepcontrol.wait;" ::: "memory");  // xs written by the X-preparation grid
 
-    float acc[1][NT][4];
+    float acc[RPW][NT][4];
+    auto zero = [&](float (&v)[RPW][NT][4]) {
 #pragma unroll
-    for (int t = 0; t < NT; ++t)
+      for (int r = 0; r < RPW; ++r)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) acc[0][t][e] = 0.0f;
-
-    const int first_tile = (int)(it0 / KS);
+        for (int t = 0; t < NT; ++t)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) v[r][t][e] = 0.0f;
+    };
+    zero(acc);
     auto slot_of = [&](int cta, int tile) -> int {
       return 2 * cta + ((int)(((long long)cta * a.T / a.G) / KS) == tile ? 0 : 1);
     };
-    auto store = [&](int tile, float (&v)[1][NT][4]) {
+    auto grp = [&](int r) { return RPW * wq + r; };  // 16-row group of row tile r within the tile
+    auto store = [&](int tile, float (&v)[RPW][NT][4]) {
 #pragma unroll
-      for (int t = 0; t < NT; ++t) {
+      for (int r = 0; r < RPW; ++r)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int n = tile * kGtRows + 16 * cw_id + g + ((e & 2) ? 8 : 0);
-          const int m = 8 * t + 2 * j + (e & 1);
-          if (n < a.N && m < a.M) {
-            float y = v[0][t][e] * __ldg(a.xs + m);
-            if (FMT == 1) y *= a.ts;
-            if (F32OUT) static_cast<float*>(a.Y)[(size_t)m * a.ldy + n] = y;
-            else if (a.tp.world > 0) tp_store(a.tp, (size_t)m, n, __float2bfloat16_rn(y));
-            else static_cast<__nv_bfloat16*>(a.Y)[(size_t)m * a.ldy + n] = __float2bfloat16_rn(y);
+        for (int t = 0; t < NT; ++t) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int n = tile * kGtRows + 16 * grp(r) + g + ((e & 2) ? 8 : 0);
+            const int m = 8 * t + 2 * j + (e & 1);
+            if (n < a.N && m < a.M) {
+              float y = v[r][t][e] * __ldg(a.xs + m);
+              if (FMT == 1) y *= a.ts;
+              if (F32OUT) static_cast<float*>(a.Y)[(size_t)m * a.ldy + n] = y;
+              else if (a.tp.world > 0) tp_store(a.tp, (size_t)m, n, __float2bfloat16_rn(y));
+              else static_cast<__nv_bfloat16*>(a.Y)[(size_t)m * a.ldy + n] = __float2bfloat16_rn(y);
+            }
           }
         }
-      }
     };
+    // Group 0 writes a finished segment: the whole tile directly, or its
+    // stream-K partial, the last contributor summing all partials in CTA order.
     auto flush = [&](int tile, bool whole) {
-      if (C::KSPLIT == 2) {  // chunk-1 warps hand their sums to the chunk-0 warps (fixed order)
-        if (kpart == 1) {
-#pragma unroll
-          for (int t = 0; t < NT; ++t)
-            s_half[(cw_id * NT + t) * 32 + lane] = make_float4(acc[0][t][0], acc[0][t][1], acc[0][t][2], acc[0][t][3]);
-        }
-        asm volatile("bar.sync 2, %0;" ::"r"(kGtCons * 32) : "memory");
-        if (kpart == 0) {
-#pragma unroll
-          for (int t = 0; t < NT; ++t) {
-            const float4 h = s_half[(cw_id * NT + t) * 32 + lane];
-            acc[0][t][0] += h.x; acc[0][t][1] += h.y; acc[0][t][2] += h.z; acc[0][t][3] += h.w;
-          }
-        }
-        asm volatile("bar.sync 2, %0;" ::"r"(kGtCons * 32) : "memory");  // s_half is reused
-        if (kpart == 1) {
-#pragma unroll
-          for (int t = 0; t < NT; ++t)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) acc[0][t][e] = 0.0f;
-          return;
-        }
-      }
       if (whole) {
         store(tile, acc);
-      } else {
-        float4* mine = reinterpret_cast<float4*>(a.partials) +
-                       ((size_t)slot_of((int)blockIdx.x, tile) * kGtGroups + cw_id) * NT * 32;
+        return;
+      }
+      float4* mine = reinterpret_cast<float4*>(a.partials) + (size_t)slot_of((int)blockIdx.x, tile) * kGtGroups * NT * 32;
+#pragma unroll
+      for (int r = 0; r < RPW; ++r)
 #pragma unroll
         for (int t = 0; t < NT; ++t)
-          __stcg(mine + t * 32 + lane, make_float4(acc[0][t][0], acc[0][t][1], acc[0][t][2], acc[0][t][3]));
+          __stcg(mine + (grp(r) * NT + t) * 32 + lane, make_float4(acc[r][t][0], acc[r][t][1], acc[r][t][2], acc[r][t][3]));
+      __threadfence();
+      asm volatile("bar.sync 1, %0;" ::"r"(WPG * 32) : "memory");
+      if (wq == 0 && lane == 0) *s_ticket = ok ? atomicAdd(a.counters + tile, 1u) : 0xFFFFFFFFu;
+      asm volatile("bar.sync 1, %0;" ::"r"(WPG * 32) : "memory");
+      const unsigned ticket = *s_ticket;
+      const long long t0 = (long long)tile * KS, t1 = t0 + KS - 1;
+      const int c_lo = (int)(((t0 + 1) * a.G - 1) / a.T), c_hi = (int)(((t1 + 1) * a.G - 1) / a.T);
+      if (ticket == (unsigned)(c_hi - c_lo)) {  // last contributor: sum in CTA order
         __threadfence();
-        asm volatile("bar.sync 1, %0;" ::"r"(kGtGroups * 32) : "memory");
-        if (cw_id == 0 && lane == 0) *s_ticket = ok ? atomicAdd(a.counters + tile, 1u) : 0xFFFFFFFFu;
-        asm volatile("bar.sync 1, %0;" ::"r"(kGtGroups * 32) : "memory");
-        const unsigned ticket = *s_ticket;
-        const long long t0 = (long long)tile * KS, t1 = t0 + KS - 1;
-        const int c_lo = (int)(((t0 + 1) * a.G - 1) / a.T), c_hi = (int)(((t1 + 1) * a.G - 1) / a.T);
-        if (ticket == (unsigned)(c_hi - c_lo)) {  // last contributor: sum in CTA order
-          __threadfence();
-          float sum[1][NT][4];
+        float sum[RPW][NT][4];
+        zero(sum);
+        for (int cc = c_lo; cc <= c_hi; ++cc) {
+          const float4* src = reinterpret_cast<const float4*>(a.partials) + (size_t)slot_of(cc, tile) * kGtGroups * NT * 32;
 #pragma unroll
-          for (int t = 0; t < NT; ++t)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) sum[0][t][e] = 0.0f;
-          for (int cc = c_lo; cc <= c_hi; ++cc) {
-            const float4* src = reinterpret_cast<const float4*>(a.partials) +
-                                ((size_t)slot_of(cc, tile) * kGtGroups + cw_id) * NT * 32;
+          for (int r = 0; r < RPW; ++r)
 #pragma unroll
             for (int t = 0; t < NT; ++t) {
-              const float4 pv = __ldcg(src + t * 32 + lane);
-              sum[0][t][0] += pv.x; sum[0][t][1] += pv.y; sum[0][t][2] += pv.z; sum[0][t][3] += pv.w;
+              const float4 pv = __ldcg(src + (grp(r) * NT + t) * 32 + lane);
+              sum[r][t][0] += pv.x; sum[r][t][1] += pv.y; sum[r][t][2] += pv.z; sum[r][t][3] += pv.w;
             }
-          }
-          store(tile, sum);
-          if (cw_id == 0 && lane == 0) a.counters[tile] = 0u;  // leave the workspace zeroed
         }
-        asm volatile("bar.sync 1, %0;" ::"r"(kGtGroups * 32) : "memory");  // s_ticket is reused
+        store(tile, sum);
+        if (wq == 0 && lane == 0) a.counters[tile] = 0u;  // leave the workspace zeroed
       }
-#pragma unroll
-      for (int t = 0; t < NT; ++t)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[0][t][e] = 0.0f;
+      asm volatile("bar.sync 1, %0;" ::"r"(WPG * 32) : "memory");  // s_ticket is reused
     };
-    (void)first_tile;
 
-    int tile = (int)(it0 / KS), ks = (int)(it0 % KS);
-    bool seg_whole = (ks == 0);
-    for (int i = 0; i < niter; ++i) {
-      const int s = i % S;
-      if (ok) ok = mbar_wait_flag(full_bar(s), (i / S) & 1, fault);
-      ok = __all_sync(0xFFFFFFFFu, ok);
-      if (ok) {
-        const uint8_t* W = gbase + W_off(s);
-        const uint8_t* X = gbase + X_off(s);
-        const uint8_t* SC = gbase + S_off(s);
+    long long it = it0;  // global index of the segment's first unit
+    int ib = 0;          // its index in this CTA's range
+    while (ib < niter) {
+      const int tile = (int)(it / KS), ks0 = (int)(it % KS);
+      const int len = (KS - ks0) < (niter - ib) ? (KS - ks0) : (niter - ib);
+      for (int i = ib + (ug - ib % UG + UG) % UG; i < ib + len; i += UG) {
+        const int s = i % S;
+        if (ok) ok = mbar_wait_flag(full_bar(s), (i / S) & 1, fault);
+        ok = __all_sync(0xFFFFFFFFu, ok);
+        if (ok) {
+          const uint8_t* W = gbase + W_off(s);
+          const uint8_t* X = gbase + X_off(s);
+          const uint8_t* SC = gbase + S_off(s);
 #pragma unroll
-        for (int cc2 = 0; cc2 < 2 / C::KSPLIT; ++cc2) {
-          const int c = (C::KSPLIT == 2) ? kpart : cc2;
-          uint32_t cw[1][2][4], cs[1][2], cx[NT][16];
+          for (int c = 0; c < 2; ++c) {  // the unit's two 128-k chunks
+            uint32_t cw[RPW][2][4], cs[RPW][2], cx[NT][16];
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int row = h ? row1 : row0;
-            const uint8_t* wr = W + row * 128;
-            if (FMT == 0) {  // 4 bytes of each of the chunk's 4 blocks
+            for (int r = 0; r < RPW; ++r)
 #pragma unroll
-              for (int b = 0; b < 4; ++b)
-                cw[0][h][b] = *reinterpret_cast<const uint32_t*>(wr + ((((uint32_t)(4 * c + b)) ^ sw) << 4) + 4 * j);
-              cs[0][h] = *reinterpret_cast<const uint32_t*>(SC + row * C::SB + 4 * c);
-            } else {         // 16 contiguous bytes
-              const uint4 v = *reinterpret_cast<const uint4*>(wr + ((((uint32_t)(4 * c + j)) ^ sw) << 4));
-              cw[0][h][0] = v.x; cw[0][h][1] = v.y; cw[0][h][2] = v.z; cw[0][h][3] = v.w;
-              cs[0][h] = *reinterpret_cast<const uint16_t*>(SC + row * C::SB + 8 * c + 2 * j);
+              for (int h = 0; h < 2; ++h) {
+                const int row = 16 * grp(r) + g + 8 * h;
+                const uint8_t* wr = W + row * 128;
+                if (FMT == 0) {  // 4 bytes of each of the chunk's 4 blocks
+#pragma unroll
+                  for (int b = 0; b < 4; ++b)
+                    cw[r][h][b] = *reinterpret_cast<const uint32_t*>(wr + ((((uint32_t)(4 * c + b)) ^ sw) << 4) + 4 * j);
+                  cs[r][h] = *reinterpret_cast<const uint32_t*>(SC + row * C::SB + 4 * c);
+                } else {         // 16 contiguous bytes
+                  const uint4 v = *reinterpret_cast<const uint4*>(wr + ((((uint32_t)(4 * c + j)) ^ sw) << 4));
+                  cw[r][h][0] = v.x; cw[r][h][1] = v.y; cw[r][h][2] = v.z; cw[r][h][3] = v.w;
+                  cs[r][h] = *reinterpret_cast<const uint16_t*>(SC + row * C::SB + 8 * c + 2 * j);
+                }
+              }
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+              const int m = 8 * t + g;
+              const uint8_t* xr = X + m * (kGtUnitK * 2);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const int idx = (FMT == 0) ? 16 * c + 4 * q + j : 16 * c + 4 * j + q;  // 8-f16 chunk of the unit
+                const uint4 v = *reinterpret_cast<const uint4*>(xr + xg_pos(FMT, idx, m) * 16);
+                cx[t][4 * q] = v.x; cx[t][4 * q + 1] = v.y; cx[t][4 * q + 2] = v.z; cx[t][4 * q + 3] = v.w;
+              }
             }
+            chunk_mma<FMT, RPW, NT>(acc, cw, cs, cx);
           }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty_bar(s));  // this warp is done with the stage
+      }
+      // the segment's sums: groups 1.. hand theirs to group 0 (fixed order)
+      if (UG > 1) {
+        if (ug != 0) {
 #pragma unroll
-          for (int t = 0; t < NT; ++t) {
-            const int m = 8 * t + g;
-            const uint8_t* xr = X + m * (kGtUnitK * 2);
+          for (int r = 0; r < RPW; ++r)
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const int idx = (FMT == 0) ? 16 * c + 4 * q + j : 16 * c + 4 * j + q;  // 8-f16 chunk of the unit
-              const int pos = (idx & ~7) | ((idx ^ m) & 7);
-              const uint4 v = *reinterpret_cast<const uint4*>(xr + pos * 16);
-              cx[t][4 * q] = v.x; cx[t][4 * q + 1] = v.y; cx[t][4 * q + 2] = v.z; cx[t][4 * q + 3] = v.w;
-            }
-          }
-          chunk_mma<FMT, 1, NT>(acc, cw, cs, cx);
+            for (int t = 0; t < NT; ++t)
+              s_part[(((ug - 1) * kGtGroups + grp(r)) * NT + t) * 32 + lane] =
+                  make_float4(acc[r][t][0], acc[r][t][1], acc[r][t][2], acc[r][t][3]);
+        }
+        asm volatile("bar.sync 2, %0;" ::"r"(kGtCons * 32) : "memory");
+        if (ug == 0) {
+          for (int gg = 1; gg < UG; ++gg)
+#pragma unroll
+            for (int r = 0; r < RPW; ++r)
+#pragma unroll
+              for (int t = 0; t < NT; ++t) {
+                const float4 h = s_part[(((gg - 1) * kGtGroups + grp(r)) * NT + t) * 32 + lane];
+                acc[r][t][0] += h.x; acc[r][t][1] += h.y; acc[r][t][2] += h.z; acc[r][t][3] += h.w;
+              }
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(empty_bar(s));  // this warp is done with the stage
-      if (ks == KS - 1 || i == niter - 1) {
-        flush(tile, seg_whole && ks == KS - 1);
-        seg_whole = true;
-      }
-      if (++ks == KS) { ks = 0; ++tile; }
+      if (ug == 0) flush(tile, ks0 == 0 && len == KS);
+      if (UG > 1) asm volatile("bar.sync 2, %0;" ::"r"(kGtCons * 32) : "memory");  // s_part is reused
+      zero(acc);
+      it += len;
+      ib += len;
     }
   }
 
@@ -377,22 +389,32 @@ size_t gemv_tma_workspace(const qgemm_weights_t* w, int sm_count) {
   return p.counter_bytes + p.partial_bytes + p.xg_bytes;
 }
 
+// Consumer layout per activation-tile count: M <= 8, three unit groups of
+// four warps with 32 rows each (measured against two and four groups: four
+// pushes the register budget to 96 and spills, two leaves too few warps to
+// hide the MMA and conversion latencies); 9 <= M <= 16, one group of eight
+// warps with 16 rows each (the register file bounds the accumulators).
+template <int NT>
+constexpr int gt_rpw() { return NT == 1 ? 2 : 1; }
+template <int NT>
+constexpr int gt_ug() { return NT == 1 ? 3 : 1; }
+
 template <int FMT, int NT, bool F32>
 static cudaError_t launch_gt_t(const CUtensorMap& mw, const GtArgs& a, cudaStream_t s) {
-  constexpr int BYTES = GtCfg<FMT, NT>::BYTES;
+  constexpr int BYTES = GtCfg<FMT, NT, gt_rpw<NT>(), gt_ug<NT>()>::BYTES;
   static bool attr[64] = {false};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr[dev]) {
-    e = cudaFuncSetAttribute(k_gemv_tma<FMT, NT, F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, BYTES);
+    e = cudaFuncSetAttribute(k_gemv_tma<FMT, NT, gt_rpw<NT>(), gt_ug<NT>(), F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, BYTES);
     if (e != cudaSuccess) return e;
     attr[dev] = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)a.G);
-  cfg.blockDim = dim3(GtCfg<FMT, NT>::THREADS);
+  cfg.blockDim = dim3(GtCfg<FMT, NT, gt_rpw<NT>(), gt_ug<NT>()>::THREADS);
   cfg.dynamicSmemBytes = BYTES;
   cfg.stream = s;
   cudaLaunchAttribute at[1];
@@ -400,7 +422,7 @@ static cudaError_t launch_gt_t(const CUtensorMap& mw, const GtArgs& a, cudaStrea
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k_gemv_tma<FMT, NT, F32>, mw, a);
+  return cudaLaunchKernelEx(&cfg, k_gemv_tma<FMT, NT, gt_rpw<NT>(), gt_ug<NT>(), F32>, mw, a);
 }
 
 // One launch over mb <= 16 activation rows whose X image (layout 2 of

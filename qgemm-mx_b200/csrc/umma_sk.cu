@@ -60,6 +60,7 @@
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
+#include "gemv_core.cuh"
 #include "tc.cuh"
 #include "tp.cuh"
 
@@ -314,12 +315,16 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
     const uint32_t w_c1 = (uint32_t)(r * 128 + (((2 * j + 1) ^ (r & 7)) << 4));
     // this thread's scale bits in a W stage: MXFP4 two E8M0 bytes, NVFP4 four E4M3 bytes
     const uint32_t sc_off = (uint32_t)(C::W_CODES + r * C::W_SCALE_ROW + (FMT == 0 ? 2 * j : 4 * j));
-    auto load_step = [&](int i, uint4& c0, uint4& c1, uint32_t& sc) -> bool {
-      const int sw = i % SW;
-      bool okw = mbar_wait_flag(fullw_bar(sw), (i / SW) & 1, fault);
+    // W ring position of the next step to load, and of the step being widened
+    int ld_s = 0, cur_s = 0;
+    uint32_t ld_ph = 0;
+    auto load_step = [&](uint4& c0, uint4& c1, uint32_t& sc, int& stage) -> bool {
+      stage = ld_s;
+      bool okw = mbar_wait_flag(fullw_bar(ld_s), ld_ph, fault);
+      if (++ld_s == SW) { ld_s = 0; ld_ph ^= 1u; }
       okw = __all_sync(0xFFFFFFFFu, okw);
       if (!okw) return false;
-      const uint8_t* st = gbase + W_off(sw);
+      const uint8_t* st = gbase + W_off(stage);
       c0 = *reinterpret_cast<const uint4*>(st + w_c0);
       c1 = *reinterpret_cast<const uint4*>(st + w_c1);
       sc = (FMT == 0) ? (uint32_t)*reinterpret_cast<const uint16_t*>(st + sc_off)
@@ -338,9 +343,11 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
     // Software pipeline: step i's codes and scales were loaded during step
     // i - 1; step i + 1's are loaded while step i's TMEM store is in flight.
     int kt = (int)(it0 % KS), seg = 0, rb = 0;
+    int sa = 0;                 // TMEM A stage of step i
+    uint32_t afree_ph = 1u;     // parity of afree_bar(sa) to wait for (from the second round on)
     uint4 c0 = make_uint4(0, 0, 0, 0), c1 = c0;
     uint32_t sc = 0;
-    if (niter > 0) ok = load_step(0, c0, c1, sc);
+    if (niter > 0) ok = load_step(c0, c1, sc, cur_s);
     for (int i = 0; i < niter && ok; ++i) {
       const bool first = (i == 0) || (kt == 0);
       if (first && i > 0) ++seg;
@@ -353,30 +360,50 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
         __syncwarp();
         if (lane == 0) mbar_arrive(basee_bar(b));
       }
-      const int sw = i % SW, sa = i % AST;
       uint32_t f0, f1, f2, f3;  // factors of the four 16-code halves of the two chunks
       if (FMT == 0) {
-        const uint32_t b0 = sc & 0xFFu, b1 = (sc >> 8) & 0xFFu;
-        f0 = f1 = (b0 == 0xFFu) ? 0x7E007E00u : f16x2_pow2((int)b0 - 127 - rb);
-        f2 = f3 = (b1 == 0xFFu) ? 0x7E007E00u : f16x2_pow2((int)b1 - 127 - rb);
+        // 2^(e - 127 - rb) is a normal f16 for e >= rb + 113 (every block
+        // within 27 binades of the segment's largest); blocks further down
+        // and NaN (0xFF) codes take the exact select chain, warp-uniformly.
+        const int b0 = (int)(sc & 0xFFu), b1 = (int)((sc >> 8) & 0xFFu);
+        const int e0 = b0 - 127 - rb, e1 = b1 - 127 - rb;
+        const bool slow = (e0 < -14) | (e1 < -14) | (b0 == 0xFF) | (b1 == 0xFF);
+        const uint32_t h0 = (uint32_t)(e0 + 15) << 10, h1 = (uint32_t)(e1 + 15) << 10;
+        f0 = f1 = h0 | (h0 << 16);
+        f2 = f3 = h1 | (h1 << 16);
+        if (__any_sync(0xFFFFFFFFu, slow)) {
+          f0 = f1 = (b0 == 0xFF) ? 0x7E007E00u : f16x2_pow2(e0);
+          f2 = f3 = (b1 == 0xFF) ? 0x7E007E00u : f16x2_pow2(e1);
+        }
       } else {
-        f0 = f16x2_e4m3(sc & 0xFFu); f1 = f16x2_e4m3((sc >> 8) & 0xFFu);
-        f2 = f16x2_e4m3((sc >> 16) & 0xFFu); f3 = f16x2_e4m3(sc >> 24);
+        // normal E4M3 codes in one step; zero / subnormal / NaN codes exactly
+        uint32_t l0, h0, l1, h1;
+        const bool ok0 = e4m3x2_to_f16x2_fast(sc & 0xFFFFu, l0, h0);
+        const bool ok1 = e4m3x2_to_f16x2_fast(sc >> 16, l1, h1);
+        const bool fast = ok0 & ok1;
+        f0 = l0; f1 = h0; f2 = l1; f3 = h1;
+        if (__any_sync(0xFFFFFFFFu, !fast)) {
+          f0 = f16x2_e4m3(sc & 0xFFu); f1 = f16x2_e4m3((sc >> 8) & 0xFFu);
+          f2 = f16x2_e4m3((sc >> 16) & 0xFFu); f3 = f16x2_e4m3(sc >> 24);
+        }
       }
       uint32_t o[32];
       widen(c0, f0, f1, o);
       widen(c1, f2, f3, o + 16);
       __syncwarp();                                   // every lane's codes are in registers:
-      if (lane == 0) mbar_arrive(emptyw_bar(sw));     // the W stage may be refilled
-      if (i >= AST) ok = mbar_wait_flag(afree_bar(sa), ((i / AST) + 1) & 1, fault);
+      if (lane == 0) mbar_arrive(emptyw_bar(cur_s));  // the W stage may be refilled
+      if (i >= AST) ok = mbar_wait_flag(afree_bar(sa), afree_ph, fault);
       ok = __all_sync(0xFFFFFFFFu, ok);
       if (!ok) break;
       tmem_st32(tmem_a + t_lane + (uint32_t)(sa * 128 + 32 * j), o);
-      if (i + 1 < niter) ok = load_step(i + 1, c0, c1, sc);  // overlaps the store
+      int nxt_s = cur_s;
+      if (i + 1 < niter) ok = load_step(c0, c1, sc, nxt_s);  // overlaps the store
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(aready_bar(sa));
+      cur_s = nxt_s;
+      if (++sa == AST) { sa = 0; afree_ph ^= 1u; }
       if (++kt == KS) kt = 0;
     }
   } else {
