@@ -121,7 +121,8 @@ size_t qgemm_workspace_size(const qgemm_weights_t* w, int32_t M);
 qgemm_status_t qgemm_workspace_init(void* workspace, size_t ws_bytes, void* stream);
 /* Number of kernel launches one qgemm_gemm_w4a16 call makes for (w, M), and
  * which GEMM kernel it uses (0 LDG-fed decode, 1 TMA-fed decode, 2 stream-K
- * tcgen05, 3 tile-per-CTA tcgen05).  Returns -1 for invalid arguments.  No
+ * tcgen05, 3 tile-per-CTA tcgen05, 4 block-scaled tcgen05 for MXFP4 with
+ * 9 <= M <= 128).  Returns -1 for invalid arguments.  No
  * counterpart in the reference (its benches launch one kernel per GEMM);
  * used for launch accounting in benchmarks. */
 int32_t qgemm_launch_count(const qgemm_weights_t* w, int32_t M, int32_t* kernel);

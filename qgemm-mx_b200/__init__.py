@@ -290,7 +290,7 @@ def workspace_size(p: Packed, M: int) -> int:
     return _lib.qgemm_workspace_size(C.byref(d), M)
 
 
-KERNEL_NAMES = {0: "k_gemv", 1: "k_gemv_tma", 2: "k_umma_sk", 3: "k_umma_ts"}
+KERNEL_NAMES = {0: "k_gemv", 1: "k_gemv_tma", 2: "k_umma_sk", 3: "k_umma_ts", 4: "k_umma_bs"}
 
 
 def launch_count(p: Packed, M: int) -> tuple[int, str]:

@@ -528,6 +528,10 @@ qgemm_status_t gemm_umma_ts(const qgemm_weights_t* w, const __half* Xh, const fl
 int umma_splits(const qgemm_weights_t* w, int M, int sm_count);
 size_t umma_split_workspace(const qgemm_weights_t* w, int M, int splits);
 
+bool umma_bs_supported(const qgemm_weights_t* w, int M);
+size_t umma_bs_workspace(const qgemm_weights_t* w, int M, int sm_count);
+qgemm_status_t gemm_umma_bs(const qgemm_weights_t* w, const uint16_t* X, int M, void* Y, bool f32, void* ws,
+                            int sm_count, cudaStream_t s, const TpOut* tp);
 bool umma_sk_supported(const qgemm_weights_t* w, int M);
 int umma_sk_bn(int M);
 size_t umma_sk_workspace(const qgemm_weights_t* w, int M, int sm_count);
@@ -591,6 +595,14 @@ qgemm_status_t gemm_decode_ex(const qgemm_weights_t* w, const uint16_t* X, int M
   const bool scales_ok = (w->format == QGEMM_FMT_NVFP4) ? (sa & 1u) == 0 : (sa & 3u) == 0;
   if (!al16(w->data) || !al16(X) || !scales_ok)
     return fail(QGEMM_ERR_INVALID_ARG, "gemm: data and X must be 16-byte aligned, scales 4-byte aligned");
+  if (umma_bs_supported(w, M)) {  // MXFP4, M <= 128: block-scaled tensor cores, no dequantisation
+    const int sms = sm_count_or_zero();
+    const size_t need = sms > 0 ? umma_bs_workspace(w, M, sms) : 0;
+    if (!ws || !al16(ws) || ws_bytes < need || need == 0)
+      return fail(QGEMM_ERR_WORKSPACE, "gemm: 16-byte aligned workspace of %zu bytes needed, %zu given", need,
+                  ws_bytes);
+    return gemm_umma_bs(w, X, M, Y, f32, ws, sms, s, tp);
+  }
   if (use_umma(w, M)) {
     const size_t need = umma_workspace(w, M);
     if (!ws || !al16(ws) || ws_bytes < need)
@@ -671,6 +683,10 @@ qgemm_status_t gemm_decode(const qgemm_weights_t* w, const uint16_t* X, int M, v
 }
 
 size_t gemm_decode_workspace(const qgemm_weights_t* w, int M) {
+  if (w && M >= 1 && umma_bs_supported(w, M)) {
+    const int sms = sm_count_or_zero();
+    return sms > 0 ? umma_bs_workspace(w, M, sms) : 0;
+  }
   if (w && use_umma(w, M)) return umma_workspace(w, M);
   if (w && M >= 1 && gemv_tma_supported(w, M < kMaxM ? M : kMaxM)) {
     const int sms = sm_count_or_zero();
@@ -690,7 +706,10 @@ size_t gemm_decode_workspace(const qgemm_weights_t* w, int M) {
 int32_t gemm_launch_count(const qgemm_weights_t* w, int M, int32_t* kernel) {
   if (!w || M < 1 || fmt_code(w->format) < 0) return -1;
   int k = 0, n = 0;
-  if (use_umma(w, M)) {
+  if (umma_bs_supported(w, M)) {
+    k = 4;
+    n = 2;  // k_xprep_bs + k_umma_bs
+  } else if (use_umma(w, M)) {
     k = umma_sk_supported(w, M) ? 2 : 3;
     n = 2;  // k_xprep + the tcgen05 kernel
   } else {

@@ -61,14 +61,16 @@ size_t gemm_decode_workspace(const qgemm_weights_t* w, int M);
 int32_t gemm_launch_count(const qgemm_weights_t* w, int M, int32_t* kernel);
 unsigned umma_sk_fault();
 unsigned gemv_tma_fault();
+unsigned umma_bs_fault();
 
 static size_t pad256_tp(size_t b) { return (b + 255) & ~(size_t)255; }
 
 // Kernels that store their slice into every rank's Y_full themselves
-// (TMA-fed decode, stream-K tcgen05); the others go through k_tp_gather.
+// (TMA-fed decode, stream-K tcgen05, block-scaled tcgen05); the others go
+// through k_tp_gather.
 static bool fused_tp(const qgemm_weights_t* w, int M) {
   int32_t k = -1;
-  return gemm_launch_count(w, M, &k) > 0 && (k == 1 || k == 2);
+  return gemm_launch_count(w, M, &k) > 0 && (k == 1 || k == 2 || k == 4);
 }
 
 }  // namespace qg
@@ -138,9 +140,10 @@ qgemm_status_t qgemm_tp_gemm_w4a16(const qgemm_weights_t* w_local, const uint16_
 qgemm_status_t qgemm_tp_status(int32_t* timed_out) {
   unsigned f = 0;
   QG_CUDA_RET(cudaMemcpyFromSymbol(&f, g_tp_fault, sizeof(f)));
-  const unsigned g = umma_sk_fault(), h = gemv_tma_fault();  // the fused kernels' own flags
-  if (g == 0xFFFFFFFFu || h == 0xFFFFFFFFu) return fail(QGEMM_ERR_CUDA, "tp_status: reading a fault flag failed");
-  f |= g | h;
+  const unsigned g = umma_sk_fault(), h = gemv_tma_fault(), b = umma_bs_fault();  // the fused kernels' own flags
+  if (g == 0xFFFFFFFFu || h == 0xFFFFFFFFu || b == 0xFFFFFFFFu)
+    return fail(QGEMM_ERR_CUDA, "tp_status: reading a fault flag failed");
+  f |= g | h | b;
   if (timed_out) *timed_out = (int32_t)f;
   return f ? fail(QGEMM_ERR_TIMEOUT, "tp_gemm: a peer did not announce its slice within 2 s") : QGEMM_OK;
 }

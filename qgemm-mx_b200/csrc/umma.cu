@@ -433,6 +433,7 @@ qgemm_status_t gemm_umma_ts(const qgemm_weights_t* w, const __half* Xh, const fl
 
 unsigned umma_sk_fault();
 unsigned gemv_tma_fault();
+unsigned umma_bs_fault();
 
 }  // namespace qg
 
@@ -443,9 +444,10 @@ extern "C" {
 qgemm_status_t qgemm_umma_status(int32_t* faulted) {
   unsigned f = 0;
   QG_CUDA_RET(cudaMemcpyFromSymbol(&f, g_umma_fault, sizeof(f)));
-  const unsigned g = umma_sk_fault(), h = gemv_tma_fault();
-  if (g == 0xFFFFFFFFu || h == 0xFFFFFFFFu) return fail(QGEMM_ERR_CUDA, "umma: reading a fault flag failed");
-  f |= g | h;
+  const unsigned g = umma_sk_fault(), h = gemv_tma_fault(), b = umma_bs_fault();
+  if (g == 0xFFFFFFFFu || h == 0xFFFFFFFFu || b == 0xFFFFFFFFu)
+    return fail(QGEMM_ERR_CUDA, "umma: reading a fault flag failed");
+  f |= g | h | b;
   if (faulted) *faulted = (int32_t)f;
   return f ? fail(QGEMM_ERR_TIMEOUT, "umma: a bounded barrier wait gave up") : QGEMM_OK;
 }
