@@ -457,23 +457,45 @@ k_umma_bs(const __grid_constant__ CUtensorMap map_w, const BsArgs a) {
         const int c_lo = (int)(((t0 + 1) * a.G - 1) / a.T), c_hi = (int)(((t1 + 1) * a.G - 1) / a.T);
         if (ticket == (unsigned)(c_hi - c_lo)) {  // last contributor: sum in CTA order
           __threadfence();
+          // The partials come from L2: up to four contributors' loads of a
+          // 16-column chunk are in flight before the first add (one load and
+          // add per contributor at a time made the tail a chain of L2 round
+          // trips).  The adds stay in CTA order.
+          constexpr int CW = BN < 16 ? BN : 16;
+          const int ncon = c_hi - c_lo + 1;
 #pragma unroll 1
-          for (int c0 = 0; c0 < BN; c0 += 8) {
-            float acc[8];
+          for (int c0 = 0; c0 < BN; c0 += CW) {
+            float acc[CW];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) acc[u] = 0.0f;
+            for (int u = 0; u < CW; ++u) acc[u] = 0.0f;
 #pragma unroll 1
-            for (int cc = c_lo; cc <= c_hi; ++cc) {
-              const int cs = 2 * cc + (tile == (int)(((long long)cc * a.T / a.G) / KS) ? 0 : 1);
-              const float4* src = reinterpret_cast<const float4*>(a.partials + (size_t)cs * (kBsRows * BN) +
-                                                                  (size_t)r * BN + c0);
-              const float4 p0 = __ldcg(src), p1 = __ldcg(src + 1);
-              acc[0] += p0.x; acc[1] += p0.y; acc[2] += p0.z; acc[3] += p0.w;
-              acc[4] += p1.x; acc[5] += p1.y; acc[6] += p1.z; acc[7] += p1.w;
+            for (int cb = 0; cb < ncon; cb += 4) {
+              float4 pv[4][CW / 4];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                if (cb + j < ncon) {
+                  const int cc = c_lo + cb + j;
+                  const int cs = 2 * cc + (tile == (int)(((long long)cc * a.T / a.G) / KS) ? 0 : 1);
+                  const float4* src = reinterpret_cast<const float4*>(a.partials + (size_t)cs * (kBsRows * BN) +
+                                                                      (size_t)r * BN + c0);
+#pragma unroll
+                  for (int u = 0; u < CW / 4; ++u) pv[j][u] = __ldcg(src + u);
+                }
+              }
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                if (cb + j < ncon) {
+#pragma unroll
+                  for (int u = 0; u < CW / 4; ++u) {
+                    acc[4 * u] += pv[j][u].x; acc[4 * u + 1] += pv[j][u].y;
+                    acc[4 * u + 2] += pv[j][u].z; acc[4 * u + 3] += pv[j][u].w;
+                  }
+                }
+              }
             }
             if (live) {
 #pragma unroll
-              for (int u = 0; u < 8; ++u) {
+              for (int u = 0; u < CW; ++u) {
                 const int m = m0 + c0 + u;
                 if (m < a.M) {
                   if (F32OUT) static_cast<float*>(a.Y)[(size_t)m * a.N + n] = acc[u];
