@@ -71,7 +71,8 @@ struct GemvArgs {
   float* partials;      // [2 * W_total][slot]
   unsigned* counters;   // [tiles]
   long long T;          // iterations = tiles * C
-  int C;                // chunks per tile
+  int C;                // chunks per tile: ceil(K / 128)
+  int ktail;            // K % 128: the last chunk's valid k (0 = a whole chunk)
   int W_total;          // warps that own iterations
 };
 
@@ -234,7 +235,13 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) k_gemv(const GemvArgs a) {
   uint32_t wq[R][2][4], sc[R][2];
   uint32_t xf[NT][16];
 
+  // Valid k of chunk c: a whole chunk, or K % 128 in the last one.  Past the
+  // end of the row the codes and X are zero and the scales neutral (finite),
+  // so those slots add nothing; nothing is read there.  With K % 128 != 0 a
+  // row's scales are not word-aligned, so they are read a byte (u16) at a time.
+  auto chunk_k = [&](int c) { return (a.ktail != 0 && c == C - 1) ? a.ktail : kChunkK; };
   auto load_w = [&](int tile, int c) {
+    const int kv = chunk_k(c);
 #pragma unroll
     for (int r = 0; r < R; ++r)
 #pragma unroll
@@ -246,28 +253,54 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) k_gemv(const GemvArgs a) {
         if (n < N) {
           const uint8_t* row = a.data + (size_t)n * rowb + (size_t)c * (kChunkK / 2);
           if constexpr (FMT == 0) {  // 4 bytes of each of the 4 blocks
+            const uint8_t* srow = static_cast<const uint8_t*>(a.scales) + (size_t)n * (K / 32) + 4 * c;
+            if (kv == kChunkK) {
 #pragma unroll
-            for (int b = 0; b < 4; ++b) wq[r][h][b] = ldg_first4(row + 16 * b + 4 * j);
-            sc[r][h] = __ldg(reinterpret_cast<const uint32_t*>(static_cast<const uint8_t*>(a.scales) +
-                                                                (size_t)n * (K / 32) + 4 * c));
+              for (int b = 0; b < 4; ++b) wq[r][h][b] = ldg_first4(row + 16 * b + 4 * j);
+            } else {
+#pragma unroll
+              for (int b = 0; b < 4; ++b)
+                if (32 * b < kv) wq[r][h][b] = ldg_first4(row + 16 * b + 4 * j);
+            }
+            if (a.ktail == 0) {
+              sc[r][h] = __ldg(reinterpret_cast<const uint32_t*>(srow));
+            } else {
+              uint32_t v = 0u;
+#pragma unroll
+              for (int b = 0; b < 4; ++b) v |= (32 * b < kv ? (uint32_t)__ldg(srow + b) : 127u) << (8 * b);
+              sc[r][h] = v;
+            }
           } else if constexpr (FMT == 3) {  // 8 bytes of each 64-group
-            const uint2 lo = ldg_stream8(row + 8 * j), hi = ldg_stream8(row + 32 + 8 * j);
-            wq[r][h][0] = lo.x; wq[r][h][1] = lo.y; wq[r][h][2] = hi.x; wq[r][h][3] = hi.y;
-            sc[r][h] = __ldg(reinterpret_cast<const uint32_t*>(static_cast<const uint16_t*>(a.scales) +
-                                                                (size_t)n * (K / 64) + 2 * c));
-          } else {  // 16 contiguous bytes
-            const uint4 v = ldg_stream16(row + 16 * j);
-            wq[r][h][0] = v.x; wq[r][h][1] = v.y; wq[r][h][2] = v.z; wq[r][h][3] = v.w;
-            if constexpr (FMT == 1)
-              sc[r][h] = __ldg(reinterpret_cast<const uint16_t*>(static_cast<const uint8_t*>(a.scales) +
-                                                                  (size_t)n * (K / 16) + 8 * c + 2 * j));
-            else
-              sc[r][h] = __ldg(static_cast<const uint16_t*>(a.scales) + (size_t)n * (K / 128) + c);
+            const uint16_t* srow = static_cast<const uint16_t*>(a.scales) + (size_t)n * (K / 64) + 2 * c;
+            const uint2 lo = ldg_stream8(row + 8 * j);
+            wq[r][h][0] = lo.x; wq[r][h][1] = lo.y;
+            if (kv == kChunkK) {
+              const uint2 hi = ldg_stream8(row + 32 + 8 * j);
+              wq[r][h][2] = hi.x; wq[r][h][3] = hi.y;
+            }
+            if (a.ktail == 0)
+              sc[r][h] = __ldg(reinterpret_cast<const uint32_t*>(srow));
+            else  // K % 64 == 0: a tail chunk holds exactly one group
+              sc[r][h] = (uint32_t)__ldg(srow) | (kv == kChunkK ? (uint32_t)__ldg(srow + 1) << 16 : 0u);
+          } else {  // 16 contiguous bytes = k 32 j .. 32 j + 31 of the chunk
+            if (32 * j < kv) {
+              const uint4 v = ldg_stream16(row + 16 * j);
+              wq[r][h][0] = v.x; wq[r][h][1] = v.y; wq[r][h][2] = v.z; wq[r][h][3] = v.w;
+              if constexpr (FMT == 1)
+                sc[r][h] = __ldg(reinterpret_cast<const uint16_t*>(static_cast<const uint8_t*>(a.scales) +
+                                                                    (size_t)n * (K / 16) + 8 * c + 2 * j));
+              else
+                sc[r][h] = __ldg(static_cast<const uint16_t*>(a.scales) + (size_t)n * (K / 128) + c);
+            } else if constexpr (FMT == 1) {
+              sc[r][h] = 0x3838u;  // E4M3 1.0 for both blocks
+            }
           }
         }
       }
   };
   auto load_x = [&](int c) {
+    const int kv = chunk_k(c);
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
       const int m = 8 * t + g;
@@ -276,13 +309,14 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) k_gemv(const GemvArgs a) {
         uint4 v[4];
         if constexpr (FMT == 0) {
 #pragma unroll
-          for (int b = 0; b < 4; ++b) v[b] = ldg_keep16(xr + 32 * b + 8 * j);
+          for (int b = 0; b < 4; ++b) v[b] = (32 * b < kv) ? ldg_keep16(xr + 32 * b + 8 * j) : z;
         } else if constexpr (FMT == 3) {
           v[0] = ldg_keep16(xr + 16 * j); v[1] = ldg_keep16(xr + 16 * j + 8);
-          v[2] = ldg_keep16(xr + 64 + 16 * j); v[3] = ldg_keep16(xr + 64 + 16 * j + 8);
+          v[2] = (kv == kChunkK) ? ldg_keep16(xr + 64 + 16 * j) : z;
+          v[3] = (kv == kChunkK) ? ldg_keep16(xr + 64 + 16 * j + 8) : z;
         } else {
 #pragma unroll
-          for (int q = 0; q < 4; ++q) v[q] = ldg_keep16(xr + 32 * j + 8 * q);
+          for (int q = 0; q < 4; ++q) v[q] = (32 * j < kv) ? ldg_keep16(xr + 32 * j + 8 * q) : z;
         }
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -464,8 +498,12 @@ qgemm_status_t gemv_plan(const qgemm_weights_t* w, int mb, GemvPlan* p) {
   const int f = fmt_code(w->format);
   if (f < 0) return fail(QGEMM_ERR_INVALID_ARG, "gemm: unknown format %d", (int)w->format);
   if (w->K == 0 || w->N == 0) return fail(QGEMM_ERR_INVALID_ARG, "gemm: empty weight matrix");
-  if (w->K % kChunkK != 0)
-    return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "gemm: K=%zu is not a multiple of %d", w->K, kChunkK);
+  // K need not be a multiple of the 128-k chunk: the last chunk may hold
+  // K % 128 valid k in whole 32-blocks (MXFP4 / NVFP4) or 64-groups (INT4 g64).
+  const size_t kq = (f == 0 || f == 1) ? 32 : (f == 3 ? 64 : 128);
+  if (w->K % kq != 0)
+    return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "gemm: K=%zu is not a multiple of %zu on the decode path%s", w->K, kq,
+                f == 1 ? " (NVFP4 rows must start on 16-byte boundaries)" : "");
   if (w->K > (size_t)INT32_MAX / 2 || w->N > (size_t)INT32_MAX / 2)
     return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "gemm: N or K too large");
   DevProps dp;
@@ -475,7 +513,7 @@ qgemm_status_t gemv_plan(const qgemm_weights_t* w, int mb, GemvPlan* p) {
   p->nt = mb <= 8 ? 1 : 2;
   p->mpad = 8 * p->nt;
   p->tiles = (int)((w->N + kTileRows - 1) / kTileRows);
-  p->C = (int)(w->K / kChunkK);
+  p->C = (int)((w->K + kChunkK - 1) / kChunkK);
   p->T = (long long)p->tiles * p->C;
   int occ = 1;
   switch (f) {
@@ -667,7 +705,7 @@ qgemm_status_t gemm_decode_ex(const qgemm_weights_t* w, const uint16_t* X, int M
     GemvPlan pb;
     st = gemv_plan(w, mb, &pb);
     if (st != QGEMM_OK) return st;
-    a.T = pb.T; a.C = pb.C; a.W_total = pb.W_total; a.M = mb;
+    a.T = pb.T; a.C = pb.C; a.ktail = (int)(w->K % kChunkK); a.W_total = pb.W_total; a.M = mb;
     a.Y = f32 ? (void*)(static_cast<float*>(Y) + (size_t)m0 * w->N)
               : (void*)(static_cast<uint16_t*>(Y) + (size_t)m0 * w->N);
     QG_CUDA_RET(launch_xprep(X + (size_t)m0 * w->K, mb, mb, (int)w->K, perm, 0, 0, xh, xs, s));
@@ -835,7 +873,7 @@ extern "C" qgemm_status_t qgemm_gemm_w4a16_noalloc(const qgemm_weights_t* w, con
     GemvPlan pb;
     st = gemv_plan(w, mb, &pb);
     if (st != QGEMM_OK) return st;
-    a.T = pb.T; a.C = pb.C; a.W_total = pb.W_total; a.M = mb;
+    a.T = pb.T; a.C = pb.C; a.ktail = (int)(w->K % kChunkK); a.W_total = pb.W_total; a.M = mb;
     a.Y = static_cast<uint16_t*>(Y) + (size_t)m0 * w->N;
     QG_CUDA_RET(launch_xprep(X + (size_t)m0 * w->K, mb, mb, (int)w->K, perm, 0, 0, xh, xs, s));
     const cudaError_t e = launch_gemv<false>(pb, a, s);
