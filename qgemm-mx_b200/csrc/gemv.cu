@@ -282,18 +282,36 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) k_gemv(const GemvArgs a) {
               sc[r][h] = __ldg(reinterpret_cast<const uint32_t*>(srow));
             else  // K % 64 == 0: a tail chunk holds exactly one group
               sc[r][h] = (uint32_t)__ldg(srow) | (kv == kChunkK ? (uint32_t)__ldg(srow + 1) << 16 : 0u);
-          } else {  // 16 contiguous bytes = k 32 j .. 32 j + 31 of the chunk
-            if (32 * j < kv) {
-              const uint4 v = ldg_stream16(row + 16 * j);
-              wq[r][h][0] = v.x; wq[r][h][1] = v.y; wq[r][h][2] = v.z; wq[r][h][3] = v.w;
-              if constexpr (FMT == 1)
-                sc[r][h] = __ldg(reinterpret_cast<const uint16_t*>(static_cast<const uint8_t*>(a.scales) +
-                                                                    (size_t)n * (K / 16) + 8 * c + 2 * j));
-              else
-                sc[r][h] = __ldg(static_cast<const uint16_t*>(a.scales) + (size_t)n * (K / 128) + c);
-            } else if constexpr (FMT == 1) {
-              sc[r][h] = 0x3838u;  // E4M3 1.0 for both blocks
+          } else if constexpr (FMT == 1) {  // 16 bytes = k 32 j .. 32 j + 31: blocks 2 j, 2 j + 1
+            const int vj = kv - 32 * j;          // valid k of the lane's 32: <= 0, 16 or >= 32
+            const uint8_t* srow = static_cast<const uint8_t*>(a.scales) + (size_t)n * (K / 16) + 8 * c + 2 * j;
+            if ((K & 31) == 0) {                 // rows start on 16-byte boundaries
+              if (vj > 0) {
+                const uint4 v = ldg_stream16(row + 16 * j);
+                wq[r][h][0] = v.x; wq[r][h][1] = v.y; wq[r][h][2] = v.z; wq[r][h][3] = v.w;
+                sc[r][h] = __ldg(reinterpret_cast<const uint16_t*>(srow));
+              } else {
+                sc[r][h] = 0x3838u;              // E4M3 1.0 for both blocks
+              }
+            } else {                             // K % 32 == 16: 8-byte rows, scale pairs unaligned
+              if (vj > 0) {
+                const uint2 lo = ldg_stream8(row + 16 * j);
+                wq[r][h][0] = lo.x; wq[r][h][1] = lo.y;
+                uint32_t s1 = 0x38u;
+                if (vj >= 32) {
+                  const uint2 hi = ldg_stream8(row + 16 * j + 8);
+                  wq[r][h][2] = hi.x; wq[r][h][3] = hi.y;
+                  s1 = __ldg(srow + 1);
+                }
+                sc[r][h] = (uint32_t)__ldg(srow) | (s1 << 8);
+              } else {
+                sc[r][h] = 0x3838u;
+              }
             }
+          } else {  // INT4 g128: 16 contiguous bytes (K % 128 == 0)
+            const uint4 v = ldg_stream16(row + 16 * j);
+            wq[r][h][0] = v.x; wq[r][h][1] = v.y; wq[r][h][2] = v.z; wq[r][h][3] = v.w;
+            sc[r][h] = __ldg(static_cast<const uint16_t*>(a.scales) + (size_t)n * (K / 128) + c);
           }
         }
       }
@@ -314,9 +332,9 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) k_gemv(const GemvArgs a) {
           v[0] = ldg_keep16(xr + 16 * j); v[1] = ldg_keep16(xr + 16 * j + 8);
           v[2] = (kv == kChunkK) ? ldg_keep16(xr + 64 + 16 * j) : z;
           v[3] = (kv == kChunkK) ? ldg_keep16(xr + 64 + 16 * j + 8) : z;
-        } else {
+        } else {  // NVFP4 / INT4 g128: k 32 j + 8 q .. + 7 (valid in whole 16-blocks)
 #pragma unroll
-          for (int q = 0; q < 4; ++q) v[q] = (32 * j < kv) ? ldg_keep16(xr + 32 * j + 8 * q) : z;
+          for (int q = 0; q < 4; ++q) v[q] = (32 * j + 8 * q < kv) ? ldg_keep16(xr + 32 * j + 8 * q) : z;
         }
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -499,11 +517,10 @@ qgemm_status_t gemv_plan(const qgemm_weights_t* w, int mb, GemvPlan* p) {
   if (f < 0) return fail(QGEMM_ERR_INVALID_ARG, "gemm: unknown format %d", (int)w->format);
   if (w->K == 0 || w->N == 0) return fail(QGEMM_ERR_INVALID_ARG, "gemm: empty weight matrix");
   // K need not be a multiple of the 128-k chunk: the last chunk may hold
-  // K % 128 valid k in whole 32-blocks (MXFP4 / NVFP4) or 64-groups (INT4 g64).
-  const size_t kq = (f == 0 || f == 1) ? 32 : (f == 3 ? 64 : 128);
+  // K % 128 valid k in whole blocks (32 MXFP4, 16 NVFP4) or 64-groups (INT4 g64).
+  const size_t kq = f == 0 ? 32 : f == 1 ? 16 : f == 3 ? 64 : 128;
   if (w->K % kq != 0)
-    return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "gemm: K=%zu is not a multiple of %zu on the decode path%s", w->K, kq,
-                f == 1 ? " (NVFP4 rows must start on 16-byte boundaries)" : "");
+    return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "gemm: K=%zu is not a multiple of %zu", w->K, kq);
   if (w->K > (size_t)INT32_MAX / 2 || w->N > (size_t)INT32_MAX / 2)
     return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "gemm: N or K too large");
   DevProps dp;

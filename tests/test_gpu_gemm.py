@@ -201,8 +201,10 @@ def test_gemm_errors(qg, cuda, O, orc):
     with pytest.raises(qg.QGemmError) as e:
         qg.gemm_w4a16(p, X, workspace=small)
     assert e.value.status == qg.ERR_WORKSPACE
-    # NVFP4 rows of K % 32 == 16 codes do not start on 16-byte boundaries
-    p2, *_ = packed_pair(qg, O, orc, "nvfp4", 16, 64, 48, seed=0)
+    # K that is not a whole number of NVFP4 blocks (the buffers are those of
+    # K = 48, larger than K = 40 needs)
+    p48, *_ = packed_pair(qg, O, orc, "nvfp4", 16, 64, 48, seed=0)
+    p2 = qg.Packed(p48.format, 64, 40, p48.data, p48.scales)
     with pytest.raises(qg.QGemmError) as e:
-        qg.gemm_w4a16(p2, torch.zeros((1, 48), dtype=torch.bfloat16, device="cuda"))
+        qg.gemm_w4a16(p2, torch.zeros((1, 40), dtype=torch.bfloat16, device="cuda"))
     assert e.value.status == qg.ERR_UNSUPPORTED_SHAPE

@@ -5,9 +5,9 @@ The reference lists them as layer archetypes (include/qgemm/shapes.hpp:27-34):
 gpt_oss_2880 (N = K = 2880, "not 128-aligned -- live bug class") and kv_gqa
 (N = 1024, K = 4096, "small N -- tails / occupancy"); its packer tests use
 K = 96 as the awkward shape (tests/test_pack_roundtrip.cpp:291-305).  K only
-has to be a multiple of the format's block (32 for MXFP4 and NVFP4 here,
-64 for INT4 g64).  The last 128-k chunk of the decode kernel then holds
-1, 2 or 3 blocks (K % 128 = 32, 64, 96), M >= 32 with K % 64 == 0 goes to
+has to be a multiple of the format's block (32 for MXFP4, 16 for NVFP4, 64
+for INT4 g64).  The last 128-k chunk of the decode kernel then holds part of
+a chunk (K % 128 = 16 .. 112), M >= 32 with K % 64 == 0 goes to
 the tcgen05 kernels, and every output is compared (tolerance of
 tests/gpu_util.py: per row max-abs <= 1e-2 ||row||_inf, relative Frobenius
 <= 1e-3; FP32 output also within 1e-5 relative Frobenius)."""
@@ -27,6 +27,9 @@ CASES = [
     ("mxfp4", 32, 300, 160, [3, 12]),                     # K % 128 = 32
     ("mxfp4", 32, 300, 224, [3, 12]),                     # K % 128 = 96
     ("nvfp4", 16, 300, 160, [2]),
+    ("nvfp4", 16, 200, 48, [1, 5, 40]),                   # K % 32 = 16: rows on 8-byte boundaries
+    ("nvfp4", 16, 200, 112, [1, 9, 33]),                  # last lane holds one 16-block
+    ("nvfp4", 16, 300, 2896, [1, 16, 40]),                # K % 128 = 80
     ("int4", 64, 300, 192, [4, 18]),                      # one 64-group in the last chunk
     ("mxfp4", 32, 1024, 4096, [1, 16, 64]),               # kv_gqa
 ]
