@@ -232,6 +232,34 @@ class ClockSampler:
                 "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
+def probe_read_gbs(qg, dev, nbytes=1 << 30):
+    """The reference's bandwidth denominator, measured in the same run: a
+    read-only stream of 128-bit loads (its src/probe/bandwidth.cu:92-97 and
+    :111-117; here qgemm_probe_launch kind 0) over a buffer 8x the L2, ten
+    launches per CUDA-graph replay, median of ten replays."""
+    import torch
+    buf = torch.ones(nbytes // 4, dtype=torch.int32, device=dev)
+    for _ in range(3):
+        qg.probe_launch(0, buf, None, nbytes)
+    torch.cuda.synchronize()
+    inner, g = 10, torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(inner):
+            qg.probe_launch(0, buf, None, nbytes)
+    samples = []
+    for _ in range(10):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        g.replay()
+        b.record()
+        b.synchronize()
+        samples.append(a.elapsed_time(b) * 1e-3 / inner)
+    qg.probe_status()
+    del g, buf
+    torch.cuda.empty_cache()
+    return nbytes / statistics.median(samples) / 1e9
+
+
 def measured_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -533,6 +561,7 @@ def main():
         del copies, g2
         torch.cuda.empty_cache()
     peak, peak_src = measured_peaks()
+    probe_gbs = probe_read_gbs(qg, dev) if rank == 0 else None
     # per GEMM kernel: algorithmic bytes per launch / mean launch time; the
     # roofline entry is the kernel with the largest share of the step
     per_kernel = {}
@@ -586,6 +615,9 @@ def main():
                                                               "(qgemm_tp_gemm_w4a16)" if world > 1 else ""),
                        "l2": "cold: step working set 419 MB > 126 MB L2, calls M-major",
                        "pct_of_hbm_peak": round(100 * value / peak, 2)},
+            "probe": {"read_only_gbs": round(probe_gbs, 1), "pct_of_probe": round(100 * value / probe_gbs, 2),
+                      "how": "qgemm_probe_launch kind 0 (128-bit loads), 1 GiB, graph of 10, median of 10; "
+                             "the reference's denominator (src/probe/bandwidth.cu:111-117), measured in this run"},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d * world,
                     "d2h_bytes_per_step": d2h * world},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
