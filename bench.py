@@ -68,6 +68,8 @@ def parse():
     ap.add_argument("--workload", default="llama70b_mxfp4", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--table", action="store_true", help="print the per-(layer, M) table to stderr")
+    ap.add_argument("--fp8", action="store_true",
+                    help="also time the cuBLASLt FP8 dense baseline on the same calls (1 GPU)")
     ap.add_argument("--prefill", action="store_true",
                     help="compute-bound table: NVFP4 (28672,8192) and (8192,28672), M in {2048,4096,8192}, "
                          "tcgen05 path vs cuBLAS BF16 of the same shape")
@@ -258,6 +260,64 @@ def probe_read_gbs(qg, dev, nbytes=1 << 30):
     del g, buf
     torch.cuda.empty_cache()
     return nbytes / statistics.median(samples) / 1e9
+
+
+def fp8_baseline(qg, dev, calls, table, l2, stream):
+    """The reference's planned "vs FP8" comparison (docs/BASELINE_STUDY.md:23,
+    docs/MASTER_EXECUTION_PLAN.md:280: MXFP4 >= 1.5x FP8 at M = 1): every call
+    of the step as a cuBLASLt FP8 GEMM (E4M3 W and X, per-tensor scales, bf16
+    Y), timed like the per-call table (weights rotated past L2, a graph of
+    launches, median of ten replays)."""
+    import torch
+    ours = {(name, M): us for name, M, N, K, rot, us, gbs, kern in table}
+    wsp = torch.empty(32 << 20, dtype=torch.uint8, device=dev)
+    one = torch.ones(1, dtype=torch.float32, device=dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(8)
+    per_call, t8, t4 = {}, 0.0, 0.0
+    w8_cache = {}
+    for M, name, N, K in calls:
+        if (N, K) not in w8_cache:
+            Wf = torch.randn((N, K), generator=gen, device=dev).mul_(0.02)
+            sw = float(Wf.abs().max()) / 448.0
+            w8_cache[(N, K)] = ((Wf / sw).to(torch.float8_e4m3fn).view(torch.uint8), torch.tensor([sw], device=dev))
+            del Wf
+        W8, sw = w8_cache[(N, K)]
+        rot = max(2, math.ceil(2 * l2 / (N * K)))
+        copies = [W8] + [W8.clone() for _ in range(rot - 1)]
+        X8 = torch.randn((M, K), generator=gen, device=dev).clamp_(-448, 448).to(torch.float8_e4m3fn).view(torch.uint8)
+        Y8 = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+        inner = max(rot, 8)
+        with torch.cuda.stream(stream):
+            for j in range(inner):
+                qg.cublaslt_fp8_gemm(copies[j % rot], X8, sw, one, out=Y8, workspace=wsp)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for j in range(inner):
+                qg.cublaslt_fp8_gemm(copies[j % rot], X8, sw, one, out=Y8, workspace=wsp)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        samples = []
+        for _ in range(10):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            g.replay()
+            b.record()
+            b.synchronize()
+            samples.append(a.elapsed_time(b) * 1e3 / inner)
+        us8 = statistics.median(samples)
+        us4 = ours[(name, M)]
+        per_call[f"{name}:M={M}"] = {"fp8_us": round(us8, 2), "mxfp4_us": round(us4, 2),
+                                     "mxfp4_vs_fp8": round(us8 / us4, 3)}
+        t8, t4 = t8 + us8, t4 + us4
+        del copies, g
+        torch.cuda.empty_cache()
+    return {"fp8_us_per_step": round(t8, 2), "mxfp4_us_per_step": round(t4, 2),
+            "mxfp4_vs_fp8": round(t8 / t4, 3), "per_call": per_call,
+            "how": "qgemm_cublaslt_fp8_gemm (cuBLASLt, E4M3 x E4M3, per-tensor scales, bf16 out), same shapes, "
+                   "weights rotated past L2, graph of launches, median of 10; mxfp4_us from the per-call table"}
 
 
 def measured_peaks():
@@ -560,6 +620,7 @@ def main():
         table.append((name, M, p.N, K, rot, us, nb / (us * 1e-6) / 1e9, kernel_of[(M, name)]))
         del copies, g2
         torch.cuda.empty_cache()
+    fp8 = fp8_baseline(qg, dev, calls, table, l2, s) if (args.fp8 and world == 1) else None
     peak, peak_src = measured_peaks()
     probe_gbs = probe_read_gbs(qg, dev) if rank == 0 else None
     # per GEMM kernel: algorithmic bytes per launch / mean launch time; the
@@ -618,6 +679,7 @@ def main():
             "probe": {"read_only_gbs": round(probe_gbs, 1), "pct_of_probe": round(100 * value / probe_gbs, 2),
                       "how": "qgemm_probe_launch kind 0 (128-bit loads), 1 GiB, graph of 10, median of 10; "
                              "the reference's denominator (src/probe/bandwidth.cu:111-117), measured in this run"},
+            **({"fp8_baseline": fp8} if fp8 else {}),
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d * world,
                     "d2h_bytes_per_step": d2h * world},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",

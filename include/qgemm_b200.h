@@ -193,6 +193,17 @@ qgemm_status_t qgemm_umma_status(int32_t* faulted);
 qgemm_status_t qgemm_cublas_bf16_gemm(const uint16_t* W, const uint16_t* X,
                                       int32_t M, size_t N, size_t K, uint16_t* Y,
                                       void* stream);
+/* cuBLASLt FP8 dense baseline, the one the reference plans for its "vs FP8"
+ * headline (docs/BASELINE_STUDY.md:23, docs/MASTER_EXECUTION_PLAN.md:121,280;
+ * no implementation there): W [N,K] and X [M,K] are E4M3 bytes, scale_w and
+ * scale_x DEVICE pointers to their FP32 per-tensor scales, Y [M,N] bf16 =
+ * (X.scale_x) . (W.scale_w)^T with FP32 accumulation.  K % 16 == 0,
+ * N % 8 == 0, W, X, Y 16-byte aligned; workspace may be null (ws_bytes 0). */
+qgemm_status_t qgemm_cublaslt_fp8_gemm(const uint8_t* W, const uint8_t* X,
+                                       int32_t M, size_t N, size_t K,
+                                       const float* scale_w, const float* scale_x,
+                                       uint16_t* Y, void* workspace, size_t ws_bytes,
+                                       void* stream);
 /* Memory probes (bandwidth.cu:25-50, bench_stream_ideal.cu:29-39).
  * kind: 0 read-only with 128-bit loads, 1 read-only with TMA bulk copies
  * (cp.async.bulk, no multicast), 2 copy src->dst, 3 write-only fill dst.

@@ -75,6 +75,7 @@ _sig("qgemm_gemm_w4a16_f32", _i32, [C.POINTER(_Weights), _vp, _i32, _vp, _vp, _s
 _sig("qgemm_gemm_w4a16_noalloc", _i32, [C.POINTER(_Weights), _vp, _i32, _vp, _vp])
 _sig("qgemm_cublas_bf16_gemm", _i32, [_vp, _vp, _i32, _sz, _sz, _vp, _vp])
 _sig("qgemm_probe_launch", _i32, [_i32, _vp, _vp, _sz, _vp])
+_sig("qgemm_cublaslt_fp8_gemm", _i32, [_vp, _vp, _i32, _sz, _sz, _vp, _vp, _vp, _vp, _sz, _vp])
 _sig("qgemm_device_info", _i32, [C.POINTER(_i32), C.POINTER(_sz)])
 _sig("qgemm_probe_status", _i32, [C.POINTER(_i32)])
 _sig("qgemm_umma_status", _i32, [C.POINTER(_i32)])
@@ -335,6 +336,23 @@ def cublas_bf16_gemm(W: torch.Tensor, X: torch.Tensor, out: torch.Tensor | None 
     if out is None:
         out = torch.empty((M, N), dtype=torch.bfloat16, device=X.device)
     _check(_lib.qgemm_cublas_bf16_gemm(_ptr(W), _ptr(X), M, N, K, _ptr(out), _stream(stream)), "cublas")
+    return out
+
+
+def cublaslt_fp8_gemm(W8: torch.Tensor, X8: torch.Tensor, scale_w: torch.Tensor, scale_x: torch.Tensor,
+                      out: torch.Tensor | None = None, workspace: torch.Tensor | None = None, stream=None):
+    """cuBLASLt FP8 dense baseline: Y[M,N] bf16 = (X8.scale_x) . (W8.scale_w)^T.
+    W8 [N,K] / X8 [M,K] hold E4M3 bytes (uint8 or float8_e4m3fn); scale_w and
+    scale_x are one-element float32 CUDA tensors."""
+    N, K = W8.shape
+    M = X8.shape[0]
+    if X8.shape[1] != K or scale_w.dtype != torch.float32 or scale_x.dtype != torch.float32:
+        raise ValueError("cublaslt_fp8_gemm: W8 [N,K], X8 [M,K], float32 scales")
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=X8.device)
+    nws = 0 if workspace is None else workspace.numel()
+    _check(_lib.qgemm_cublaslt_fp8_gemm(_ptr(W8), _ptr(X8), M, N, K, _ptr(scale_w), _ptr(scale_x), _ptr(out),
+                                        _ptr(workspace), nws, _stream(stream)), "cublaslt_fp8_gemm")
     return out
 
 

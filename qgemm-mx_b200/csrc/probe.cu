@@ -7,6 +7,7 @@
 // (cp.async.bulk global->shared, completion on an mbarrier, no multicast).
 // Every mbarrier wait is bounded by %globaltimer; a timeout sets a device
 // flag that qgemm_probe_launch reports on the next call instead of hanging.
+#include <cublasLt.h>
 #include <cublas_v2.h>
 
 #include "common.cuh"
@@ -174,6 +175,72 @@ qgemm_status_t qgemm_probe_status(int32_t* timed_out) {
   QG_CUDA_RET(cudaMemcpyFromSymbol(&flag, g_probe_timeout, sizeof(flag)));
   if (timed_out) *timed_out = (int32_t)flag;
   return flag ? fail(QGEMM_ERR_TIMEOUT, "probe: a TMA bulk probe wait timed out") : QGEMM_OK;
+}
+
+// One cuBLASLt handle per device and host thread.
+static cublasLtHandle_t lt_handle() {
+  static thread_local cublasLtHandle_t h[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!h[dev] && cublasLtCreate(&h[dev]) != CUBLAS_STATUS_SUCCESS) h[dev] = nullptr;
+  return h[dev];
+}
+
+qgemm_status_t qgemm_cublaslt_fp8_gemm(const uint8_t* W, const uint8_t* X, int32_t M, size_t N, size_t K,
+                                       const float* scale_w, const float* scale_x, uint16_t* Y, void* workspace,
+                                       size_t ws_bytes, void* stream) {
+  auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+  if (!W || !X || !Y || !scale_w || !scale_x || M < 1 || N == 0 || K == 0 || K % 16 != 0 || N % 8 != 0 ||
+      !al16(W) || !al16(X) || !al16(Y) || (ws_bytes && !workspace) || K > (size_t)INT32_MAX ||
+      N > (size_t)INT32_MAX)
+    return fail(QGEMM_ERR_INVALID_ARG,
+                "cublaslt_fp8_gemm: bad arguments (K %% 16 == 0, N %% 8 == 0, 16-byte aligned W, X, Y)");
+  cublasLtHandle_t h = lt_handle();
+  if (!h) return fail(QGEMM_ERR_CUDA, "cublaslt_fp8_gemm: cublasLtCreate failed");
+  cublasLtMatmulDesc_t op = nullptr;
+  cublasLtMatrixLayout_t la = nullptr, lb = nullptr, lc = nullptr;
+  cublasLtMatmulPreference_t pref = nullptr;
+  qgemm_status_t st = QGEMM_OK;
+  auto ok = [&](cublasStatus_t c, const char* what) {
+    if (c != CUBLAS_STATUS_SUCCESS && st == QGEMM_OK)
+      st = fail(QGEMM_ERR_CUDA, "cublaslt_fp8_gemm: %s failed (%d)", what, (int)c);
+    return c == CUBLAS_STATUS_SUCCESS;
+  };
+  // Y_rm[M,N] = X_rm[M,K] . W_rm[N,K]^T  ==  C_cm[N,M] = op_T(W_cm[K,N]) . X_cm[K,M]
+  // (FP8 operands: both K-major, the "TN" form), per-tensor scales on the device.
+  const cublasOperation_t ta = CUBLAS_OP_T, tb = CUBLAS_OP_N;
+  if (ok(cublasLtMatmulDescCreate(&op, CUBLAS_COMPUTE_32F, CUDA_R_32F), "MatmulDescCreate") &&
+      ok(cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_TRANSA, &ta, sizeof(ta)), "TRANSA") &&
+      ok(cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_TRANSB, &tb, sizeof(tb)), "TRANSB") &&
+      ok(cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_A_SCALE_POINTER, &scale_w, sizeof(scale_w)),
+         "A_SCALE_POINTER") &&
+      ok(cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_B_SCALE_POINTER, &scale_x, sizeof(scale_x)),
+         "B_SCALE_POINTER") &&
+      ok(cublasLtMatrixLayoutCreate(&la, CUDA_R_8F_E4M3, K, N, (int64_t)K), "layout W") &&
+      ok(cublasLtMatrixLayoutCreate(&lb, CUDA_R_8F_E4M3, K, (uint64_t)M, (int64_t)K), "layout X") &&
+      ok(cublasLtMatrixLayoutCreate(&lc, CUDA_R_16BF, N, (uint64_t)M, (int64_t)N), "layout Y") &&
+      ok(cublasLtMatmulPreferenceCreate(&pref), "PreferenceCreate") &&
+      ok(cublasLtMatmulPreferenceSetAttribute(pref, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES, &ws_bytes,
+                                              sizeof(ws_bytes)), "MAX_WORKSPACE_BYTES")) {
+    cublasLtMatmulHeuristicResult_t res = {};
+    int found = 0;
+    if (ok(cublasLtMatmulAlgoGetHeuristic(h, op, la, lb, lc, lc, pref, 1, &res, &found), "AlgoGetHeuristic")) {
+      if (found < 1) {
+        st = fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "cublaslt_fp8_gemm: no algorithm for M=%d N=%zu K=%zu", (int)M, N, K);
+      } else {
+        const float alpha = 1.0f, beta = 0.0f;
+        ok(cublasLtMatmul(h, op, &alpha, W, la, X, lb, &beta, Y, lc, Y, lc, &res.algo, workspace, ws_bytes,
+                          as_stream(stream)),
+           "Matmul");
+      }
+    }
+  }
+  if (pref) cublasLtMatmulPreferenceDestroy(pref);
+  if (lc) cublasLtMatrixLayoutDestroy(lc);
+  if (lb) cublasLtMatrixLayoutDestroy(lb);
+  if (la) cublasLtMatrixLayoutDestroy(la);
+  if (op) cublasLtMatmulDescDestroy(op);
+  return st;
 }
 
 qgemm_status_t qgemm_cublas_bf16_gemm(const uint16_t* W, const uint16_t* X, int32_t M, size_t N, size_t K,
