@@ -760,6 +760,12 @@ size_t gemm_decode_workspace(const qgemm_weights_t* w, int M) {
 // Mirrors gemm_decode's dispatch: launches per call and the GEMM kernel used.
 int32_t gemm_launch_count(const qgemm_weights_t* w, int M, int32_t* kernel) {
   if (!w || M < 1 || fmt_code(w->format) < 0) return -1;
+  {  // the shapes the GEMM entry accepts (gemv_plan's checks, which every call makes first)
+    const int f = fmt_code(w->format);
+    const size_t kq = f == 0 ? 32 : f == 1 ? 16 : f == 3 ? 64 : 128;
+    if (w->K == 0 || w->N == 0 || w->K % kq != 0 || w->K > (size_t)INT32_MAX / 2 || w->N > (size_t)INT32_MAX / 2)
+      return -1;
+  }
   int k = 0, n = 0;
   if (umma_bs_supported(w, M)) {
     k = 4;

@@ -115,3 +115,11 @@ def test_launch_count_mirrors_dispatch(qg):
     assert count(qg.INT4_G64, 8192, 8192, 64) == (8, "k_gemv")
     w = qg._Weights(qg.MXFP4, 0, 64, 256, None, None, 1.0)
     assert lib.qgemm_launch_count(C.byref(w), 0, C.byref(kern)) == -1
+    # K only needs each format's own divisibility; the rest is refused as the GEMM refuses it
+    assert count(qg.MXFP4, 2880, 2880, 1) == (2, "k_gemv")          # gpt_oss 2880: K % 128 = 64
+    assert count(qg.MXFP4, 2880, 2880, 33) == (2, "k_umma_ts")
+    assert count(qg.NVFP4, 200, 48, 1) == (2, "k_gemv")             # K % 32 = 16
+    assert count(qg.INT4_G64, 2880, 2880, 20) == (4, "k_gemv")
+    assert count(qg.INT4_G128, 2880, 2880, 1)[0] == -1              # 2880 % 128 != 0
+    assert count(qg.MXFP4, 64, 48, 1)[0] == -1                      # not whole 32-blocks
+    assert count(qg.NVFP4, 64, 40, 1)[0] == -1
