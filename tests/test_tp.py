@@ -1,7 +1,7 @@
 """Tensor-parallel path: W sharded along N over the GPUs of one node, each
 rank computing its Y slice and the slices gathered into every rank's Y.
 
-CPU (gloo, world size 2): the sharding the multi-GPU path relies on -- a
+CPU (gloo, world sizes 2, 4, 8): the sharding the multi-GPU path relies on -- a
 rank's shard of packed W is a contiguous slice of the full packing's data
 and scales, its Y slice is the full GEMM's column block, and the gathered
 slices are the full result -- checked with the oracle; plus the C-ABI's
@@ -29,7 +29,7 @@ def _free_port():
 
 
 # ---------------------------------------------------------------------------
-# CPU: sharding with the oracle, two gloo ranks
+# CPU: sharding with the oracle, 2 / 4 / 8 gloo ranks
 # ---------------------------------------------------------------------------
 
 def _cpu_rank(rank, world, port, fmt, N, K, M, out):
@@ -59,10 +59,12 @@ def _cpu_rank(rank, world, port, fmt, N, K, M, out):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("fmt,N,K,M", [("mxfp4", 256, 512, 3), ("nvfp4", 128, 256, 1)])
-def test_shards_are_row_slices_and_gather_to_full_result(O, orc, fmt, N, K, M):
+@pytest.mark.parametrize("fmt,N,K,M,world", [("mxfp4", 256, 512, 3, 2), ("nvfp4", 128, 256, 1, 2),
+                                              ("mxfp4", 256, 512, 3, 4), ("mxfp4", 1024, 256, 2, 8)])
+def test_shards_are_row_slices_and_gather_to_full_result(O, orc, fmt, N, K, M, world):
+    """World sizes of the scaling runs (2, 4, 8): every rank's packed shard is
+    its contiguous row slice and the gathered Y equals the full result."""
     import torch.multiprocessing as mp
-    world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
