@@ -81,6 +81,7 @@ def parse():
 def run_case(args):
     """One GEMM configuration launched --warmup + --steps times (eager, one
     weight buffer); used for ncu captures of a single kernel."""
+    import ctypes as C
     import torch
     qg = importlib.import_module("qgemm-mx_b200")
     fmt, N, K, M = args.case.split(",")
@@ -105,7 +106,10 @@ def run_case(args):
     torch.cuda.synchronize()
     us = a.elapsed_time(b) * 1e3 / args.steps
     nb = qg.total_bytes(fcode, M, N, K)
-    print(json.dumps({"case": args.case, "us_per_call": round(us, 3), "gbs": round(nb / us / 1e3, 1)}))
+    f = C.c_int32(0)
+    qg.lib().qgemm_umma_status(C.byref(f))  # nonzero: a bounded wait gave up (times and outputs invalid)
+    print(json.dumps({"case": args.case, "us_per_call": round(us, 3), "gbs": round(nb / us / 1e3, 1),
+                      "wait_timed_out": bool(f.value)}))
 
 
 def run_prefill(args):
@@ -686,6 +690,9 @@ def main():
         del copies, g2
         torch.cuda.empty_cache()
     fp8 = fp8_baseline(qg, dev, calls, table, l2, s) if (args.fp8 and world == 1) else None
+    # no number is reported from a run in which a kernel's bounded wait gave up
+    # (its outputs are then wrong): that raises here and the bench exits non-zero
+    qg.umma_status()
     peak, peak_src = measured_peaks()
     probe_gbs = probe_read_gbs(qg, dev) if rank == 0 else None
     # per GEMM kernel: algorithmic bytes per launch / mean launch time; the
