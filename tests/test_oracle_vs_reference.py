@@ -85,3 +85,22 @@ def test_w4a16_cpu_path(O, orc, ref, fmt, group):
     Wd = ref.dequant(fmt, d, s, N, K, group=group, tensor_scale=ts)
     c = ref.gemm_ref(O.bf16_bits_to_f32(X), Wd)
     assert np.array_equal(a.view(np.uint32), c.view(np.uint32))
+
+
+@pytest.mark.parametrize("fmt,group,K", [("mxfp4", 32, 96), ("mxfp4", 32, 2880), ("nvfp4", 16, 48),
+                                         ("nvfp4", 16, 112), ("nvfp4", 16, 2880), ("int4", 64, 192),
+                                         ("int4", 64, 2880)])
+def test_unaligned_k_pack_and_cpu_path(O, orc, ref, fmt, group, K):
+    """K that is a whole number of the format's blocks but not of 128 (the
+    reference's gpt_oss_2880 and K = 96 shapes, shapes.hpp:33,
+    test_pack_roundtrip.cpp:291-305): packing and the W4A16 CPU path stay
+    bit-identical to the reference's."""
+    N, M = 24, 2
+    W = weights(O, N, K, seed=K)
+    ts = O.nvfp4_tensor_scale(W) if fmt == "nvfp4" else 1.0
+    st, d, s = _packs(orc, ref, W, fmt, group=group, tensor_scale=ts)
+    assert st == 0
+    X = O.randn_bf16(1, 2, M * K).reshape(M, K)
+    a = orc.w4a16_gemm(fmt, d, s, N, K, X, group=group, tensor_scale=ts, nthreads=2)
+    b = ref.w4a16_gemm(fmt, d, s, N, K, X, group=group, tensor_scale=ts, nthreads=2)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
