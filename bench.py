@@ -53,6 +53,7 @@ WORKLOADS = {
     "llama70b_mxfp4": ("mxfp4", [("qkv", 10240, 8192), ("gate_up", 57344, 8192), ("down", 8192, 28672)],
                        [1, 8, 32, 64]),
     "decode_14336x4096": ("nvfp4", [("gate_up", 14336, 4096)], [1, 4, 8, 16]),
+    "decode_14336x4096_int4": ("int4", [("gate_up", 14336, 4096)], [1, 4, 8, 16]),
     "llama8b_mxfp4": ("mxfp4", [("qkv", 6144, 4096), ("o_proj", 4096, 4096), ("gate_up", 28672, 4096),
                                 ("down", 4096, 14336)], [1, 2, 4, 8, 16, 32, 64, 128, 256]),
 }

@@ -287,11 +287,34 @@ k_umma_ts(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUt
         if (s_ticket == (unsigned)(a.splits - 1)) {
           __threadfence();
           const float* base = a.partials + tile_lin * a.splits * (size_t)(BN * kUBM);
+          // 16 columns at a time with up to two splits' loads in flight
+          // before the first add (they come from L2; one load and add per
+          // column and split made this a chain of BN x splits round trips);
+          // the adds stay in split order
 #pragma unroll 1
-          for (int c = 0; c < BN; ++c) {
-            float acc = 0.0f;
-            for (int z = 0; z < a.splits; ++z) acc += __ldcg(base + (size_t)z * (BN * kUBM) + (size_t)c * kUBM + r);
-            store(m0 + c, acc);
+          for (int c0 = 0; c0 < BN; c0 += 16) {
+            float acc[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) acc[i] = 0.0f;
+#pragma unroll 1
+            for (int z0 = 0; z0 < a.splits; z0 += 2) {
+              float pv[2][16];
+#pragma unroll
+              for (int j = 0; j < 2; ++j)
+                if (z0 + j < a.splits) {
+#pragma unroll
+                  for (int i = 0; i < 16; ++i)
+                    pv[j][i] = __ldcg(base + (size_t)(z0 + j) * (BN * kUBM) + (size_t)(c0 + i) * kUBM + r);
+                }
+#pragma unroll
+              for (int j = 0; j < 2; ++j)
+                if (z0 + j < a.splits) {
+#pragma unroll
+                  for (int i = 0; i < 16; ++i) acc[i] += pv[j][i];
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) store(m0 + c0 + i, acc[i]);
           }
           if (warp == 2 && lane == 0) a.counters[tile_lin] = 0u;  // leave the workspace zeroed
         }
