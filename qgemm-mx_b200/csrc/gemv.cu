@@ -405,14 +405,32 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) k_gemv(const GemvArgs a) {
           for (int t = 0; t < NT; ++t)
 #pragma unroll
             for (int e = 0; e < 4; ++e) sum[r][t][e] = 0.0f;
-        for (int ww = w_lo; ww <= w_hi; ++ww) {
-          const float4* src = reinterpret_cast<const float4*>(a.partials) + slot_of(ww, tile) * (FRAG / 4) * 32;
+        // CB contributors' partials in flight before the first add (they
+        // come from L2); the adds stay in warp order
+        constexpr int CB = NT == 1 ? 4 : 2;
+#pragma unroll 1
+        for (int wb = w_lo; wb <= w_hi; wb += CB) {
+          float4 pv[CB][R][NT];
 #pragma unroll
-          for (int r = 0; r < R; ++r)
+          for (int j = 0; j < CB; ++j)
+            if (wb + j <= w_hi) {
+              const float4* src =
+                  reinterpret_cast<const float4*>(a.partials) + slot_of(wb + j, tile) * (FRAG / 4) * 32;
 #pragma unroll
-            for (int t = 0; t < NT; ++t) {
-              const float4 p = __ldcg(src + ((r * NT + t) * 32 + lane));
-              sum[r][t][0] += p.x; sum[r][t][1] += p.y; sum[r][t][2] += p.z; sum[r][t][3] += p.w;
+              for (int r = 0; r < R; ++r)
+#pragma unroll
+                for (int t = 0; t < NT; ++t) pv[j][r][t] = __ldcg(src + ((r * NT + t) * 32 + lane));
+            }
+#pragma unroll
+          for (int j = 0; j < CB; ++j)
+            if (wb + j <= w_hi) {
+#pragma unroll
+              for (int r = 0; r < R; ++r)
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                  sum[r][t][0] += pv[j][r][t].x; sum[r][t][1] += pv[j][r][t].y;
+                  sum[r][t][2] += pv[j][r][t].z; sum[r][t][3] += pv[j][r][t].w;
+                }
             }
         }
         store_tile(tile, sum);
