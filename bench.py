@@ -63,11 +63,12 @@ FALLBACK_HBM_GBS = 6650.0
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="llama70b_mxfp4", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-cublas", action="store_true", help="skip the cuBLAS BF16 column of the per-call table")
     ap.add_argument("--table", action="store_true", help="print the per-(layer, M) table to stderr")
     ap.add_argument("--fp8", action="store_true",
                     help="also time the cuBLASLt FP8 dense baseline on the same calls (1 GPU)")
@@ -239,20 +240,21 @@ class ClockSampler:
                 "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
-def probe_read_gbs(qg, dev, nbytes=1 << 30):
+def probe_read_gbs(qg, dev, kind=0, nbytes=1 << 30):
     """The reference's bandwidth denominator, measured in the same run: a
-    read-only stream of 128-bit loads (its src/probe/bandwidth.cu:92-97 and
-    :111-117; here qgemm_probe_launch kind 0) over a buffer 8x the L2, ten
-    launches per CUDA-graph replay, median of ten replays."""
+    read-only stream over a buffer 8x the L2 (its src/probe/bandwidth.cu:92-97
+    and :111-117), ten launches per CUDA-graph replay, median of ten replays.
+    kind 0: 128-bit loads; kind 1: TMA bulk copies into shared memory (no
+    multicast)."""
     import torch
     buf = torch.ones(nbytes // 4, dtype=torch.int32, device=dev)
     for _ in range(3):
-        qg.probe_launch(0, buf, None, nbytes)
+        qg.probe_launch(kind, buf, None, nbytes)
     torch.cuda.synchronize()
     inner, g = 10, torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
         for _ in range(inner):
-            qg.probe_launch(0, buf, None, nbytes)
+            qg.probe_launch(kind, buf, None, nbytes)
     samples = []
     for _ in range(10):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -274,7 +276,7 @@ def fp8_baseline(qg, dev, calls, table, l2, stream):
     Y), timed like the per-call table (weights rotated past L2, a graph of
     launches, median of ten replays)."""
     import torch
-    ours = {(name, M): us for name, M, N, K, rot, us, gbs, kern in table}
+    ours = {(r["layer"], r["M"]): r["cold_us"] for r in table}
     wsp = torch.empty(32 << 20, dtype=torch.uint8, device=dev)
     one = torch.ones(1, dtype=torch.float32, device=dev)
     gen = torch.Generator(device=dev)
@@ -325,6 +327,131 @@ def fp8_baseline(qg, dev, calls, table, l2, stream):
                    "weights rotated past L2, graph of launches, median of 10; X is given already in E4M3 (its "
                    "quantisation is not timed, while mxfp4_us includes the X preparation kernel); mxfp4_us from "
                    "the per-call table"}
+
+
+def _median_us(run_once, inner, samples=20):
+    """Median over `samples` of (device time of run_once()) / inner, in us."""
+    import torch
+    out = []
+    for _ in range(samples):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        run_once()
+        b.record()
+        b.synchronize()
+        out.append(a.elapsed_time(b) * 1e3 / inner)
+    return statistics.median(out)
+
+
+def time_graphed(fn, inner, stream):
+    """The reference's time_graphed (timing.cuh:288-336): `inner` calls
+    fn(j) captured into one CUDA graph, warmed, median of replays, per call."""
+    import torch
+    with torch.cuda.stream(stream):
+        for j in range(inner):
+            fn(j)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for j in range(inner):
+            fn(j)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    us = _median_us(g.replay, inner)
+    del g
+    return us
+
+
+def time_looped(fn, inner, stream):
+    """The reference's time_looped (timing.cuh:250-277): the same calls
+    launched one by one from the host, so launch overhead is inside."""
+    import torch
+    with torch.cuda.stream(stream):
+        for j in range(inner):
+            fn(j)
+        torch.cuda.synchronize()
+
+        def loop():
+            for j in range(inner):
+                fn(j)
+        us = _median_us(loop, inner)
+    return us
+
+
+def per_call_table(qg, dev, calls, shards, X, Y, ws, fcode, l2, stream, kernel_of, cublas=True):
+    """Per (layer, M), as the reference's bench_cublas.cu:152-175 reports:
+    cold = graphed with the weights rotated past L2 (rot = max(2, ceil(2 L2 /
+    W bytes)), timing.cuh:152-158, inner = max(rot, 8)); hot = graphed on one
+    weight buffer; looped = the cold calls launched one by one;
+    l2_inflation = cold / hot; launch_share = 100 (looped - cold) / looped;
+    GB/s and %% of peak from the algorithmic bytes (formats.cuh:80-83);
+    TFLOP/s = 2 M N K / cold and its fraction of the measured BF16 peak; and a
+    cuBLAS BF16 GEMM of the same shape (dense bf16 W, rotated likewise)."""
+    import torch
+    peak_hbm, _ = measured_peaks()
+    bf16_peak = measured_bf16_tflops()
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(99)
+    wb16 = {}
+    rows = []
+    for M, name, N, K in calls:
+        p = shards[name]
+        wbytes = qg.weight_bytes(fcode, p.N, K)
+        rot = max(2, math.ceil(2 * l2 / max(wbytes, 1)))
+        copies = [p] + [qg.Packed(p.format, p.N, p.K, p.data.clone(), p.scales.clone(), p.tensor_scale)
+                        for _ in range(rot - 1)]
+        inner = max(rot, 8)
+        Xm, Ym, wsm = X[(M, K)], Y[(M, name)], ws[(M, name)]
+
+        def cold(j):
+            qg.gemm_w4a16(copies[j % rot], Xm, out=Ym, workspace=wsm)
+
+        def hot(j):
+            qg.gemm_w4a16(p, Xm, out=Ym, workspace=wsm)
+        c_us = time_graphed(cold, inner, stream)
+        h_us = time_graphed(hot, inner, stream)
+        l_us = time_looped(cold, inner, stream)
+        nb = qg.total_bytes(fcode, M, p.N, K)
+        fl = 2.0 * M * p.N * K
+        r = {"layer": name, "M": M, "N": p.N, "K": K, "rot": rot, "kernel": kernel_of[(M, name)],
+             "cold_us": round(c_us, 3), "hot_us": round(h_us, 3), "looped_us": round(l_us, 3),
+             "bytes": nb, "gbs": round(nb / (c_us * 1e-6) / 1e9, 1),
+             "pct_of_hbm_peak": round(100 * nb / (c_us * 1e-6) / 1e9 / peak_hbm, 2),
+             "tflops": round(fl / (c_us * 1e-6) / 1e12, 2),
+             "frac_of_bf16_peak": round(fl / (c_us * 1e-6) / 1e12 / bf16_peak, 4),
+             "l2_inflation": round(c_us / h_us, 3), "launch_share_pct": round(100 * (l_us - c_us) / l_us, 2)}
+        del copies
+        if cublas:
+            key = (p.N, K)
+            if key not in wb16:
+                wb16.clear()
+                torch.cuda.empty_cache()
+                wb16[key] = torch.randn((p.N, K), generator=gen, device=dev).mul_(0.02).to(torch.bfloat16)
+            W16 = wb16[key]
+            rot16 = max(2, math.ceil(2 * l2 / (2 * p.N * K)))
+            c16 = [W16] + [W16.clone() for _ in range(rot16 - 1)]
+            Yc = torch.empty((M, p.N), dtype=torch.bfloat16, device=dev)
+
+            def cub(j):
+                qg.cublas_bf16_gemm(c16[j % rot16], Xm, out=Yc)
+            cu_us = time_graphed(cub, max(rot16, 8), stream)
+            r["cublas_bf16_us"] = round(cu_us, 3)
+            r["vs_cublas_bf16"] = round(cu_us / c_us, 3)
+            del c16, Yc
+        rows.append(r)
+        torch.cuda.empty_cache()
+    wb16.clear()
+    torch.cuda.empty_cache()
+    return rows
+
+
+def measured_bf16_tflops():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"])
+    return 1590.0
 
 
 def measured_peaks():
@@ -624,6 +751,9 @@ def main():
 
     e2e_run(max(3, args.warmup))
     torch.cuda.synchronize()
+    # the end-to-end run is captured as one graph of all its steps: bounded so
+    # the capture stays small (the device-side region above runs --steps)
+    e2e_steps = min(args.steps, 100)
     g_e2e = None
     if world == 1:
         # the whole run (every step's copies in and out and its 12 C-ABI calls)
@@ -631,7 +761,7 @@ def main():
         # does not pace the GPU; one untimed replay, then the timed one
         g_e2e = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g_e2e):
-            e2e_run(args.steps)
+            e2e_run(e2e_steps)
         g_e2e.replay()
         torch.cuda.synchronize()
     if world > 1:
@@ -641,7 +771,7 @@ def main():
     if g_e2e is not None:
         g_e2e.replay()
     else:
-        e2e_run(args.steps)
+        e2e_run(e2e_steps)
     e1.record()
     torch.cuda.synchronize()
     if world == 1:  # the read-backs of the last step equal a fresh call (the kernels are deterministic)
@@ -649,62 +779,31 @@ def main():
             ref_y = qg.gemm_w4a16(shards[name], Xd[(M, K)].copy_(Xh[(M, K)]), workspace=ws[(M, name)])
             if not torch.equal(ref_y.cpu().view(torch.int16), Yh[(M, name)].view(torch.int16)):
                 raise SystemExit(f"e2e: read-back of {name} M={M} differs from a fresh call")
-    te = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
+    te = torch.tensor([e0.elapsed_time(e1) / e2e_steps], device=dev)
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_value = bytes_step / (float(te.item()) * 1e-3) / 1e9
 
-    # ---- roofline of the decode kernel: per (layer, M), rotated, graphed ---
-    table = []
-    ktime, kbytes = 0.0, 0
-    for M, name, N, K in calls:
-        p = shards[name]
-        wbytes = qg.weight_bytes(fcode, p.N, K)
-        rot = max(2, math.ceil(2 * l2 / max(wbytes, 1)))
-        copies = [p] + [qg.Packed(p.format, p.N, p.K, p.data.clone(), p.scales.clone(), p.tensor_scale)
-                        for _ in range(rot - 1)]
-        inner = max(rot, 8)
-        g2 = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(s):
-            for j in range(inner):
-                qg.gemm_w4a16(copies[j % rot], X[(M, K)], out=Y[(M, name)], workspace=ws[(M, name)])
-        torch.cuda.synchronize()
-        with torch.cuda.graph(g2):
-            for j in range(inner):
-                qg.gemm_w4a16(copies[j % rot], X[(M, K)], out=Y[(M, name)], workspace=ws[(M, name)])
-        for _ in range(3):
-            g2.replay()
-        torch.cuda.synchronize()
-        samples = []
-        for _ in range(10):
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            g2.replay()
-            b.record()
-            b.synchronize()
-            samples.append(a.elapsed_time(b) * 1e3 / inner)  # us per launch-set
-        us = statistics.median(samples)
-        nb = qg.total_bytes(fcode, M, p.N, K)
-        ktime += us * 1e-6
-        kbytes += nb
-        table.append((name, M, p.N, K, rot, us, nb / (us * 1e-6) / 1e9, kernel_of[(M, name)]))
-        del copies, g2
-        torch.cuda.empty_cache()
+    # ---- per-call table: the reference's protocol (bench_cublas.cu:152-175) --
+    table = per_call_table(qg, dev, calls, shards, X, Y, ws, fcode, l2, s, kernel_of,
+                           cublas=(world == 1 and not args.no_cublas))
     fp8 = fp8_baseline(qg, dev, calls, table, l2, s) if (args.fp8 and world == 1) else None
     # no number is reported from a run in which a kernel's bounded wait gave up
     # (its outputs are then wrong): that raises here and the bench exits non-zero
     qg.umma_status()
     peak, peak_src = measured_peaks()
-    probe_gbs = probe_read_gbs(qg, dev) if rank == 0 else None
+    probe_ldg = probe_read_gbs(qg, dev, 0) if rank == 0 else None
+    probe_tma = probe_read_gbs(qg, dev, 1) if rank == 0 else None
+    probe_gbs = max(probe_ldg, probe_tma) if rank == 0 else None
     # per GEMM kernel: algorithmic bytes per launch / mean launch time; the
     # roofline entry is the kernel with the largest share of the step
     per_kernel = {}
-    for name, M, N, K, rot, us, gbs, kern in table:
-        d = per_kernel.setdefault(kern, {"us": 0.0, "bytes": 0, "launches": 0, "shapes": []})
-        d["us"] += us
-        d["bytes"] += qg.total_bytes(fcode, M, N, K)
+    for r in table:
+        d = per_kernel.setdefault(r["kernel"], {"us": 0.0, "bytes": 0, "launches": 0, "shapes": []})
+        d["us"] += r["cold_us"]
+        d["bytes"] += r["bytes"]
         d["launches"] += 1
-        d["shapes"].append(f"{name}:M={M}")
+        d["shapes"].append(f"{r['layer']}:M={r['M']}")
     dom = max(per_kernel, key=lambda k: per_kernel[k]["us"])
     achieved = per_kernel[dom]["bytes"] / (per_kernel[dom]["us"] * 1e-6) / 1e9
     traffic = None
@@ -732,9 +831,14 @@ def main():
                          f"{reps} passes, {secs:.1f} s"}
 
     if args.table and rank == 0:
-        print(f"{'layer':8s} {'M':>4s} {'N':>6s} {'K':>6s} {'rot':>3s} {'us':>9s} {'GB/s':>8s}  kernel", file=sys.stderr)
-        for name, M, N, K, rot, us, gbs, kern in table:
-            print(f"{name:8s} {M:4d} {N:6d} {K:6d} {rot:3d} {us:9.2f} {gbs:8.1f}  {kern}", file=sys.stderr)
+        print(f"{'layer':8s} {'M':>4s} {'N':>6s} {'K':>6s} {'rot':>3s} {'cold_us':>9s} {'hot_us':>8s} "
+              f"{'loop_us':>8s} {'GB/s':>8s} {'%peak':>6s} {'TF/s':>7s} {'l2inf':>6s} {'launch%':>7s} "
+              f"{'cublas':>8s}  kernel", file=sys.stderr)
+        for r in table:
+            print(f"{r['layer']:8s} {r['M']:4d} {r['N']:6d} {r['K']:6d} {r['rot']:3d} {r['cold_us']:9.2f} "
+                  f"{r['hot_us']:8.2f} {r['looped_us']:8.2f} {r['gbs']:8.1f} {100 * r['gbs'] / peak:6.1f} "
+                  f"{r['tflops']:7.1f} {r['l2_inflation']:6.2f} {r['launch_share_pct']:7.1f} "
+                  f"{(r.get('cublas_bf16_us') or 0):8.2f}  {r['kernel']}", file=sys.stderr)
 
     if rank == 0:
         line = {
@@ -750,11 +854,16 @@ def main():
                        "l2": "cold: step working set 419 MB > 126 MB L2, calls M-major",
                        "pct_of_hbm_peak": round(100 * value / peak, 2)},
             "probe": {"read_only_gbs": round(probe_gbs, 1), "pct_of_probe": round(100 * value / probe_gbs, 2),
-                      "how": "qgemm_probe_launch kind 0 (128-bit loads), 1 GiB, graph of 10, median of 10; "
-                             "the reference's denominator (src/probe/bandwidth.cu:111-117), measured in this run"},
+                      "ldg_gbs": round(probe_ldg, 1), "tma_bulk_gbs": round(probe_tma, 1),
+                      "how": "max of qgemm_probe_launch kinds 0 (128-bit loads) and 1 (TMA bulk copies), "
+                             "1 GiB, graph of 10, median of 10; the reference's denominator "
+                             "(src/probe/bandwidth.cu:111-117), measured in this run"},
+            "per_call": [{k: v for k, v in r.items() if k != "bytes"} for r in table],
+            "per_call_how": "cold/hot/looped as the reference's bench_cublas.cu:152-175 (graph of max(rot, 8) "
+                            "calls, median of 20); cublas_bf16_us: dense bf16 W of the same shape, rotated",
             **({"fp8_baseline": fp8} if fp8 else {}),
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d * world,
-                    "d2h_bytes_per_step": d2h * world},
+                    "d2h_bytes_per_step": d2h * world, "steps": e2e_steps},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
                          "kernel": dom, "share": round(per_kernel[dom]["us"] / sum(v["us"] for v in per_kernel.values()), 3),

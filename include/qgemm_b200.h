@@ -187,6 +187,18 @@ qgemm_status_t qgemm_gemm_w4a16_noalloc(const qgemm_weights_t* w, const uint16_t
  * wait inside the tcgen05 GEMM kernel gave up on this device.  Not capturable. */
 qgemm_status_t qgemm_umma_status(int32_t* faulted);
 
+/* Synchronous: waits for the device, then resets every fault flag of the
+ * current device (the GEMM kernels', the tensor-parallel exchange's and the
+ * TMA probe's).  No counterpart in the reference, whose errors are fatal
+ * (timing.cuh:36-44).  After a call that reported QGEMM_ERR_TIMEOUT its
+ * outputs are wrong; the GEMM workspaces need nothing (every contributor of a
+ * split tile takes its ticket even after a timeout, so the tickets return to
+ * zero), but the tp sync blocks of every rank must be zeroed again
+ * (qgemm_workspace_init) before the next tp call, since a rank that gave up
+ * is a call ahead of its peers.  Then call this and continue.  Not
+ * capturable. */
+qgemm_status_t qgemm_clear_faults(void);
+
 /* ---- baselines and probes (bench harness; not on the product path) ------- */
 /* cuBLAS BF16 dense Y[M,N] = X[M,K] . W[N,K]^T (bench_cublas.cu:144-151 with
  * CUDA_R_16BF in place of CUDA_R_16F, COMPUTE_32F). */

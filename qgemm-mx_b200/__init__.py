@@ -79,6 +79,7 @@ _sig("qgemm_cublaslt_fp8_gemm", _i32, [_vp, _vp, _i32, _sz, _sz, _vp, _vp, _vp, 
 _sig("qgemm_device_info", _i32, [C.POINTER(_i32), C.POINTER(_sz)])
 _sig("qgemm_probe_status", _i32, [C.POINTER(_i32)])
 _sig("qgemm_umma_status", _i32, [C.POINTER(_i32)])
+_sig("qgemm_clear_faults", _i32, [])
 _sig("qgemm_tp_sync_bytes", _sz, [_i32])
 _sig("qgemm_tp_workspace_size", _sz, [C.POINTER(_Weights), _i32])
 _sig("qgemm_tp_gemm_w4a16", _i32, [C.POINTER(_Weights), C.c_void_p, _i32, _i32, _i32, C.POINTER(C.c_void_p),
@@ -370,6 +371,12 @@ def umma_status() -> None:
     """Raises QGemmError if a bounded wait inside the tcgen05 kernel gave up."""
     f = _i32(0)
     _check(_lib.qgemm_umma_status(C.byref(f)), "umma_status")
+
+
+def clear_faults() -> None:
+    """Waits for the device and resets its fault flags (after a reported
+    timeout; tp sync blocks must be zeroed again first)."""
+    _check(_lib.qgemm_clear_faults(), "clear_faults")
 
 
 # ---- tensor parallel (W sharded along N over the GPUs of one node) ------------

@@ -48,6 +48,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <atomic>
+
 #include "common.cuh"
 #include "gemv_core.cuh"
 #include "tp.cuh"
@@ -569,6 +571,35 @@ qgemm_status_t gemv_plan(const qgemm_weights_t* w, int mb, GemvPlan* p) {
   return QGEMM_OK;
 }
 
+// Scratch of the LDG-fed path for a call over M activation rows, launched
+// in blocks of 16 rows: [counters | partials | xs | Xh].  A tail block of
+// M % 16 rows plans on its own (<= 8 rows: one n-tile, its own occupancy and
+// warp count), so the partial region is sized for the larger of the first
+// block's and the tail block's plans; every launch checks its plan against it.
+struct LdgLayout {
+  GemvPlan first;
+  size_t partial_bytes = 0;  // reserved partial region
+  size_t total = 0;
+};
+static qgemm_status_t ldg_layout(const qgemm_weights_t* w, int M, LdgLayout* L) {
+  qgemm_status_t st = gemv_plan(w, M < kMaxM ? M : kMaxM, &L->first);
+  if (st != QGEMM_OK) return st;
+  L->partial_bytes = L->first.partial_bytes;
+  if (M > kMaxM && (M % kMaxM) != 0) {
+    GemvPlan tail;
+    st = gemv_plan(w, M % kMaxM, &tail);
+    if (st != QGEMM_OK) return st;
+    if (tail.partial_bytes > L->partial_bytes) L->partial_bytes = tail.partial_bytes;
+  }
+  L->total = L->first.counter_bytes + L->partial_bytes + L->first.xs_bytes + L->first.xh_bytes;
+  return QGEMM_OK;
+}
+
+// Launches of the LDG-fed path over all M rows, in blocks of 16, with the
+// scratch at `base` laid out by L.
+static qgemm_status_t ldg_run(const qgemm_weights_t* w, const uint16_t* X, int M, void* Y, bool f32,
+                              uint8_t* base, const LdgLayout& L, cudaStream_t s, const char* who);
+
 template <int FMT, bool F32>
 static cudaError_t launch_fmt(const GemvPlan& p, const GemvArgs& a, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
@@ -722,30 +753,41 @@ qgemm_status_t gemm_decode_ex(const qgemm_weights_t* w, const uint16_t* X, int M
     return QGEMM_OK;
   }
   if (tp) return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "gemm: no tensor-parallel output on this path");
-  if (!ws || !al16(ws) || ws_bytes < p.total())
-    return fail(QGEMM_ERR_WORKSPACE, "gemm: 16-byte aligned workspace of %zu bytes needed, %zu given", p.total(),
+  LdgLayout L;
+  st = ldg_layout(w, M, &L);
+  if (st != QGEMM_OK) return st;
+  if (!ws || !al16(ws) || ws_bytes < L.total)
+    return fail(QGEMM_ERR_WORKSPACE, "gemm: 16-byte aligned workspace of %zu bytes needed, %zu given", L.total,
                 ws_bytes);
-  uint8_t* base = static_cast<uint8_t*>(ws);
+  return ldg_run(w, X, M, Y, f32, static_cast<uint8_t*>(ws), L, s, "gemm");
+}
+
+static qgemm_status_t ldg_run(const qgemm_weights_t* w, const uint16_t* X, int M, void* Y, bool f32,
+                              uint8_t* base, const LdgLayout& L, cudaStream_t s, const char* who) {
+  const GemvPlan& p = L.first;
   GemvArgs a;
   a.data = w->data; a.scales = w->scales; a.N = (int)w->N; a.K = (int)w->K; a.ldy = (int)w->N;
   a.ts = w->tensor_scale;
   a.counters = reinterpret_cast<unsigned*>(base);
   a.partials = reinterpret_cast<float*>(base + p.counter_bytes);
-  float* xs = reinterpret_cast<float*>(base + p.counter_bytes + p.partial_bytes);
-  __half* xh = reinterpret_cast<__half*>(base + p.counter_bytes + p.partial_bytes + p.xs_bytes);
+  float* xs = reinterpret_cast<float*>(base + p.counter_bytes + L.partial_bytes);
+  __half* xh = reinterpret_cast<__half*>(base + p.counter_bytes + L.partial_bytes + p.xs_bytes);
   a.xs = xs; a.Xh = xh;
   const int perm = (w->format == QGEMM_FMT_INT4_G128 || w->format == QGEMM_FMT_INT4_G64) ? 1 : 0;
   for (int m0 = 0; m0 < M; m0 += kMaxM) {
     const int mb = (M - m0) < kMaxM ? (M - m0) : kMaxM;
     GemvPlan pb;
-    st = gemv_plan(w, mb, &pb);
+    qgemm_status_t st = gemv_plan(w, mb, &pb);
     if (st != QGEMM_OK) return st;
+    if (pb.partial_bytes > L.partial_bytes || pb.counter_bytes != p.counter_bytes)
+      return fail(QGEMM_ERR_WORKSPACE, "%s: block plan needs %zu partial bytes, %zu reserved", who,
+                  pb.partial_bytes, L.partial_bytes);
     a.T = pb.T; a.C = pb.C; a.ktail = (int)(w->K % kChunkK); a.W_total = pb.W_total; a.M = mb;
     a.Y = f32 ? (void*)(static_cast<float*>(Y) + (size_t)m0 * w->N)
               : (void*)(static_cast<uint16_t*>(Y) + (size_t)m0 * w->N);
     QG_CUDA_RET(launch_xprep(X + (size_t)m0 * w->K, mb, mb, (int)w->K, perm, 0, 0, xh, xs, s));
     const cudaError_t e = f32 ? launch_gemv<true>(pb, a, s) : launch_gemv<false>(pb, a, s);
-    if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "gemm: launch failed: %s", cudaGetErrorString(e));
+    if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "%s: launch failed: %s", who, cudaGetErrorString(e));
   }
   return QGEMM_OK;
 }
@@ -765,14 +807,9 @@ size_t gemm_decode_workspace(const qgemm_weights_t* w, int M) {
     const int sms = sm_count_or_zero();
     return sms > 0 ? decode_tma_workspace(w, sms) : 0;
   }
-  GemvPlan p;
-  if (!w || M < 1 || gemv_plan(w, M < kMaxM ? M : kMaxM, &p) != QGEMM_OK) return 0;
-  size_t need = p.total();
-  if (M > kMaxM && (M % kMaxM) != 0) {  // the tail block may plan differently
-    GemvPlan q;
-    if (gemv_plan(w, M % kMaxM, &q) == QGEMM_OK && q.total() > need) need = q.total();
-  }
-  return need;
+  LdgLayout L;
+  if (!w || M < 1 || ldg_layout(w, M, &L) != QGEMM_OK) return 0;
+  return L.total;
 }
 
 // Mirrors gemm_decode's dispatch: launches per call and the GEMM kernel used.
@@ -844,9 +881,13 @@ qgemm_status_t qgemm_gemm_w4a16_f32(const qgemm_weights_t* w, const uint16_t* X,
 // Properties:
 //  * 16 MiB of device memory per GPU that loads the library, held until the
 //    process exits.  Calls whose plan needs more scratch (about K > 300k, or a
-//    device with far more SMs) return QGEMM_ERR_WORKSPACE.
+//    device with far more SMs) return QGEMM_ERR_WORKSPACE; the check covers
+//    every 16-row block of the call, the tail block's own plan included.
 //  * The first call on each device looks up the array's device address with
-//    cudaGetSymbolAddress; make that first call before any stream capture.
+//    cudaGetSymbolAddress and keeps it for the life of the process; make that
+//    first call before any stream capture.  cudaDeviceReset destroys the
+//    context the address belongs to: a process that resets a device must not
+//    call this entry point on that device again.
 //  * Every call shares the array: calls that may overlap on the GPU (other
 //    streams, other threads) race and must be serialised by the caller.
 //  * The tile tickets that must start at zero are cleared by each call
@@ -858,19 +899,23 @@ namespace qg {
 constexpr size_t kNoAllocScratchBytes = (size_t)16 << 20;
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
+// The array's device address per device ordinal.  Threads that race on the
+// first lookup store the same value; the atomics make that well defined.
 static qgemm_status_t noalloc_scratch(uint8_t** out) {
-  static uint8_t* ptrs[64] = {nullptr};
+  static std::atomic<uint8_t*> ptrs[64];
   int dev = 0;
   QG_CUDA_RET(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return fail(QGEMM_ERR_CUDA, "gemm_noalloc: device ordinal %d out of range", dev);
-  if (!ptrs[dev]) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || !p)
+  uint8_t* p = ptrs[dev].load(std::memory_order_acquire);
+  if (!p) {
+    void* q = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&q, g_noalloc_scratch);
+    if (e != cudaSuccess || !q)
       return fail(QGEMM_ERR_CUDA, "gemm_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
-    ptrs[dev] = static_cast<uint8_t*>(p);
+    p = static_cast<uint8_t*>(q);
+    ptrs[dev].store(p, std::memory_order_release);
   }
-  *out = ptrs[dev];
+  *out = p;
   return QGEMM_OK;
 }
 
@@ -886,39 +931,19 @@ extern "C" qgemm_status_t qgemm_gemm_w4a16_noalloc(const qgemm_weights_t* w, con
   if (w->reserved != 0) return fail(QGEMM_ERR_INVALID_ARG, "gemm_noalloc: reserved field must be 0");
   if (w->format == QGEMM_FMT_NVFP4 && !std::isfinite(w->tensor_scale))
     return fail(QGEMM_ERR_INVALID_ARG, "gemm_noalloc: NVFP4 tensor_scale must be finite");
-  GemvPlan p;
-  qgemm_status_t st = gemv_plan(w, M < kMaxM ? M : kMaxM, &p);
+  LdgLayout L;
+  qgemm_status_t st = ldg_layout(w, M, &L);
   if (st != QGEMM_OK) return st;
   const uintptr_t sa = reinterpret_cast<uintptr_t>(w->scales);
   const bool scales_ok = (w->format == QGEMM_FMT_NVFP4) ? (sa & 1u) == 0 : (sa & 3u) == 0;
   if (!al16(w->data) || !al16(X) || !scales_ok)
     return fail(QGEMM_ERR_INVALID_ARG, "gemm_noalloc: data and X must be 16-byte aligned, scales 4-byte aligned");
-  if (p.total() > kNoAllocScratchBytes)
+  if (L.total > kNoAllocScratchBytes)
     return fail(QGEMM_ERR_WORKSPACE, "gemm_noalloc: needs %zu bytes of scratch, the fixed array holds %zu",
-                p.total(), kNoAllocScratchBytes);
+                L.total, kNoAllocScratchBytes);
   uint8_t* base = nullptr;
   st = noalloc_scratch(&base);
   if (st != QGEMM_OK) return st;
-  QG_CUDA_RET(cudaMemsetAsync(base, 0, p.counter_bytes, s));
-  GemvArgs a;
-  a.data = w->data; a.scales = w->scales; a.N = (int)w->N; a.K = (int)w->K; a.ldy = (int)w->N;
-  a.ts = w->tensor_scale;
-  a.counters = reinterpret_cast<unsigned*>(base);
-  a.partials = reinterpret_cast<float*>(base + p.counter_bytes);
-  float* xs = reinterpret_cast<float*>(base + p.counter_bytes + p.partial_bytes);
-  __half* xh = reinterpret_cast<__half*>(base + p.counter_bytes + p.partial_bytes + p.xs_bytes);
-  a.xs = xs; a.Xh = xh;
-  const int perm = (w->format == QGEMM_FMT_INT4_G128 || w->format == QGEMM_FMT_INT4_G64) ? 1 : 0;
-  for (int m0 = 0; m0 < M; m0 += kMaxM) {
-    const int mb = (M - m0) < kMaxM ? (M - m0) : kMaxM;
-    GemvPlan pb;
-    st = gemv_plan(w, mb, &pb);
-    if (st != QGEMM_OK) return st;
-    a.T = pb.T; a.C = pb.C; a.ktail = (int)(w->K % kChunkK); a.W_total = pb.W_total; a.M = mb;
-    a.Y = static_cast<uint16_t*>(Y) + (size_t)m0 * w->N;
-    QG_CUDA_RET(launch_xprep(X + (size_t)m0 * w->K, mb, mb, (int)w->K, perm, 0, 0, xh, xs, s));
-    const cudaError_t e = launch_gemv<false>(pb, a, s);
-    if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "gemm_noalloc: launch failed: %s", cudaGetErrorString(e));
-  }
-  return QGEMM_OK;
+  QG_CUDA_RET(cudaMemsetAsync(base, 0, L.first.counter_bytes, s));
+  return ldg_run(w, X, M, Y, false, base, L, s, "gemm_noalloc");
 }

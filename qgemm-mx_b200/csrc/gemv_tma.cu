@@ -236,7 +236,7 @@ k_gemv_tma(const __grid_constant__ CUtensorMap map_w, const GtArgs a) {
           __stcg(mine + (grp(r) * NT + t) * 32 + lane, make_float4(acc[r][t][0], acc[r][t][1], acc[r][t][2], acc[r][t][3]));
       __threadfence();
       asm volatile("bar.sync 1, %0;" ::"r"(WPG * 32) : "memory");
-      if (wq == 0 && lane == 0) *s_ticket = ok ? atomicAdd(a.counters + tile, 1u) : 0xFFFFFFFFu;
+      if (wq == 0 && lane == 0) *s_ticket = atomicAdd(a.counters + tile, 1u);  // also after a timeout: the tickets still return to zero
       asm volatile("bar.sync 1, %0;" ::"r"(WPG * 32) : "memory");
       const unsigned ticket = *s_ticket;
       const long long t0 = (long long)tile * KS, t1 = t0 + KS - 1;
@@ -466,6 +466,11 @@ qgemm_status_t gemm_gemv_tma(const qgemm_weights_t* w, const __half* xg, const f
 size_t gemv_tma_xg_offset(const qgemm_weights_t* w, int sm_count) {
   const GtPlan p = gt_plan(w, 16, sm_count);
   return p.counter_bytes + p.partial_bytes;
+}
+
+cudaError_t gemv_tma_fault_clear() {
+  const unsigned z = 0;
+  return cudaMemcpyToSymbol(g_gemv_tma_fault, &z, sizeof(z));
 }
 
 unsigned gemv_tma_fault() {

@@ -17,6 +17,11 @@ namespace qg {
 __device__ unsigned g_probe_timeout = 0;
 __device__ unsigned g_probe_sink = 0;
 
+cudaError_t probe_fault_clear() {
+  const unsigned z = 0;
+  return cudaMemcpyToSymbol(g_probe_timeout, &z, sizeof(z));
+}
+
 __global__ void k_read16(const uint4* __restrict__ in, size_t n4) {
   const size_t stride = (size_t)gridDim.x * blockDim.x;
   uint32_t acc = 0;

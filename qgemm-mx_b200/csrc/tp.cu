@@ -63,6 +63,11 @@ unsigned umma_sk_fault();
 unsigned gemv_tma_fault();
 unsigned umma_bs_fault();
 
+cudaError_t tp_fault_clear() {
+  const unsigned z = 0;
+  return cudaMemcpyToSymbol(g_tp_fault, &z, sizeof(z));
+}
+
 static size_t pad256_tp(size_t b) { return (b + 255) & ~(size_t)255; }
 
 // Kernels that store their slice into every rank's Y_full themselves

@@ -282,7 +282,7 @@ k_umma_ts(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUt
         __shared__ unsigned s_ticket;
         __threadfence();
         asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (warp == 2 && lane == 0) s_ticket = ok ? atomicAdd(a.counters + tile_lin, 1u) : 0xFFFFFFFFu;
+        if (warp == 2 && lane == 0) s_ticket = atomicAdd(a.counters + tile_lin, 1u);  // also after a timeout: the tickets still return to zero
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (s_ticket == (unsigned)(a.splits - 1)) {
           __threadfence();
@@ -457,6 +457,11 @@ qgemm_status_t gemm_umma_ts(const qgemm_weights_t* w, const __half* Xh, const fl
 unsigned umma_sk_fault();
 unsigned gemv_tma_fault();
 unsigned umma_bs_fault();
+cudaError_t umma_sk_fault_clear();
+cudaError_t gemv_tma_fault_clear();
+cudaError_t umma_bs_fault_clear();
+cudaError_t tp_fault_clear();
+cudaError_t probe_fault_clear();
 
 }  // namespace qg
 
@@ -473,6 +478,18 @@ qgemm_status_t qgemm_umma_status(int32_t* faulted) {
   f |= g | h | b;
   if (faulted) *faulted = (int32_t)f;
   return f ? fail(QGEMM_ERR_TIMEOUT, "umma: a bounded barrier wait gave up") : QGEMM_OK;
+}
+
+qgemm_status_t qgemm_clear_faults(void) {
+  QG_CUDA_RET(cudaDeviceSynchronize());  // no kernel may still be setting a flag
+  const unsigned z = 0;
+  QG_CUDA_RET(cudaMemcpyToSymbol(g_umma_fault, &z, sizeof(z)));
+  QG_CUDA_RET(umma_sk_fault_clear());
+  QG_CUDA_RET(gemv_tma_fault_clear());
+  QG_CUDA_RET(umma_bs_fault_clear());
+  QG_CUDA_RET(tp_fault_clear());
+  QG_CUDA_RET(probe_fault_clear());
+  return QGEMM_OK;
 }
 
 }  // extern "C"

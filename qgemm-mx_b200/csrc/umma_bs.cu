@@ -450,7 +450,7 @@ k_umma_bs(const __grid_constant__ CUtensorMap map_w, const BsArgs a) {
         // every epilogue warp takes the same named-barrier steps, also after a timeout
         __threadfence();
         asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (warp == kBsEpiWarp0 && lane == 0) *s_ticket = ok ? atomicAdd(a.counters + tile, 1u) : 0xFFFFFFFFu;
+        if (warp == kBsEpiWarp0 && lane == 0) *s_ticket = atomicAdd(a.counters + tile, 1u);  // also after a timeout: the tickets still return to zero
         asm volatile("bar.sync 1, 128;" ::: "memory");
         const unsigned ticket = *s_ticket;
         const long long t0 = (long long)tile * KS, t1 = t0 + KS - 1;
@@ -672,6 +672,11 @@ qgemm_status_t gemm_umma_bs(const qgemm_weights_t* w, const uint16_t* X, int M, 
   const cudaError_t e = f32 ? launch_bs<true>(p.bn, mw, a, s) : launch_bs<false>(p.bn, mw, a, s);
   if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "block-scaled launch: %s", cudaGetErrorString(e));
   return QGEMM_OK;
+}
+
+cudaError_t umma_bs_fault_clear() {
+  const unsigned z = 0;
+  return cudaMemcpyToSymbol(g_bs_fault, &z, sizeof(z));
 }
 
 unsigned umma_bs_fault() {

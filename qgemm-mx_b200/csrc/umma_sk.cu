@@ -495,7 +495,7 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
         // every epilogue warp takes the same named-barrier steps, also after a timeout
         __threadfence();
         asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (warp == kSkEpiWarp0 && lane == 0) *s_ticket = ok ? atomicAdd(a.counters + tile, 1u) : 0xFFFFFFFFu;
+        if (warp == kSkEpiWarp0 && lane == 0) *s_ticket = atomicAdd(a.counters + tile, 1u);  // also after a timeout: the tickets still return to zero
         asm volatile("bar.sync 1, 128;" ::: "memory");
         const unsigned ticket = *s_ticket;
         const long long t0 = (long long)tile * KS, t1 = t0 + KS - 1;
@@ -660,6 +660,11 @@ qgemm_status_t gemm_umma_sk(const qgemm_weights_t* w, const __half* Xh, const fl
     e = f32 ? launch_sk_bn<1, true>(p.bn, mw, a, s) : launch_sk_bn<1, false>(p.bn, mw, a, s);
   if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "stream-K tcgen05 launch: %s", cudaGetErrorString(e));
   return QGEMM_OK;
+}
+
+cudaError_t umma_sk_fault_clear() {
+  const unsigned z = 0;
+  return cudaMemcpyToSymbol(g_sk_fault, &z, sizeof(z));
 }
 
 unsigned umma_sk_fault() {
