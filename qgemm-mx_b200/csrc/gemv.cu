@@ -644,13 +644,10 @@ qgemm_status_t gemm_umma_sk(const qgemm_weights_t* w, const __half* Xh, const fl
 
 bool gemv_tma_supported(const qgemm_weights_t* w, int mb);
 size_t gemv_tma_workspace(const qgemm_weights_t* w, int sm_count);
-size_t gemv_tma_xg_offset(const qgemm_weights_t* w, int sm_count);
-qgemm_status_t gemm_gemv_tma(const qgemm_weights_t* w, const __half* xg, const float* xs, int mb, void* Y, int ldy,
-                             bool f32, void* ws, int sm_count, cudaStream_t s, const TpOut* tp);
-// [xs (16 floats) | counters | partials | X image]
-static size_t decode_tma_workspace(const qgemm_weights_t* w, int sms) {
-  return pad256((size_t)kMaxM * sizeof(float)) + gemv_tma_workspace(w, sms);
-}
+qgemm_status_t gemm_gemv_tma(const qgemm_weights_t* w, const uint16_t* X, int mb, void* Y, int ldy, bool f32,
+                             void* ws, int sm_count, cudaStream_t s, const TpOut* tp);
+// [counters | partials | X image] (gemv_tma.cu)
+static size_t decode_tma_workspace(const qgemm_weights_t* w, int sms) { return gemv_tma_workspace(w, sms); }
 
 // The tcgen05 paths (dequantised W in TMEM) take MXFP4 / NVFP4 with M >= 32:
 // the persistent stream-K kernel for M < 128 and K % 256 == 0 (umma_sk.cu),
@@ -725,28 +722,24 @@ qgemm_status_t gemm_decode_ex(const qgemm_weights_t* w, const uint16_t* X, int M
     return gemm_umma_ts(w, xh, xs, M, Y, f32, umma_split_count(w, M), split_ws, s);
   }
   if (gemv_tma_supported(w, M < kMaxM ? M : kMaxM)) {
-    // TMA-fed decode kernel (gemv_tma.cu), one launch per 16 activation rows
+    // TMA-fed decode kernel (gemv_tma.cu): X preparation + GEMM per 16
+    // activation rows
     const int sms = sm_count_or_zero();
     const size_t need = decode_tma_workspace(w, sms);
     if (sms <= 0 || !ws || !al16(ws) || ws_bytes < need)
       return fail(QGEMM_ERR_WORKSPACE, "gemm: 16-byte aligned workspace of %zu bytes needed, %zu given", need,
                   ws_bytes);
-    float* xs = static_cast<float*>(ws);
-    uint8_t* tws = static_cast<uint8_t*>(ws) + pad256((size_t)kMaxM * sizeof(float));
-    __half* xg = reinterpret_cast<__half*>(tws + gemv_tma_xg_offset(w, sms));
     for (int m0 = 0; m0 < M; m0 += kMaxM) {
       const int mb = (M - m0) < kMaxM ? (M - m0) : kMaxM;
-      const int mpad = mb <= 8 ? 8 : 16;
-      QG_CUDA_RET(launch_xprep(X + (size_t)m0 * w->K, mb, mpad, (int)w->K, 0,
-                               w->format == QGEMM_FMT_NVFP4 ? 3 : 2, mpad, xg, xs, s));
+      const uint16_t* Xb = X + (size_t)m0 * w->K;
       if (tp) {  // this block's rows of every rank's Y_full
         TpOut tb = *tp;
         for (int d = 0; d < tb.world; ++d) tb.y[d] += (size_t)m0 * tb.ldy;
-        st = gemm_gemv_tma(w, xg, xs, mb, nullptr, 0, false, tws, sms, s, &tb);
+        st = gemm_gemv_tma(w, Xb, mb, nullptr, 0, false, ws, sms, s, &tb);
       } else {
         void* Yb = f32 ? (void*)(static_cast<float*>(Y) + (size_t)m0 * w->N)
                        : (void*)(static_cast<uint16_t*>(Y) + (size_t)m0 * w->N);
-        st = gemm_gemv_tma(w, xg, xs, mb, Yb, (int)w->N, f32, tws, sms, s, nullptr);
+        st = gemm_gemv_tma(w, Xb, mb, Yb, (int)w->N, f32, ws, sms, s, nullptr);
       }
       if (st != QGEMM_OK) return st;
     }
@@ -830,7 +823,7 @@ int32_t gemm_launch_count(const qgemm_weights_t* w, int M, int32_t* kernel) {
     n = 2;  // k_xprep + the tcgen05 kernel
   } else {
     k = gemv_tma_supported(w, M < kMaxM ? M : kMaxM) ? 1 : 0;
-    n = 2 * ((M + kMaxM - 1) / kMaxM);  // per 16 activation rows: k_xprep + decode kernel
+    n = 2 * ((M + kMaxM - 1) / kMaxM);  // per 16 activation rows: X preparation + decode kernel
   }
   if (kernel) *kernel = k;
   return n;

@@ -9,6 +9,18 @@
 // SM keeps a deep shared-memory ring full with TMA, so HBM sees enough
 // requests in flight to run near its peak.
 //
+// X is prepared once per call by k_xprep_units, one warp per (activation
+// row, 256-k unit): f16 scaled by a power of two 2^-s per row and unit, with
+// the row's largest |x| in the unit in [2^14, 2^15), so every bf16 value at or
+// above 2^-29 of that largest converts exactly (its 8 significant bits fit
+// f16's 11) and smaller ones round to f16's subnormal grid.  The unit's image
+// and its row factors 2^s are one contiguous block the producers bulk-copy
+// beside the weights.  The consumers sum each unit into a partial and add
+// partial * 2^s into the FP32 accumulator (one FMA by an exact power of two),
+// so Y differs from the double-accumulated reference (ref_gemm.hpp:15-27)
+// only by FP32 summation order.  Per-unit rather than per-row factors make the
+// preparation one parallel pass with no row-wide reduction.
+//
 // Unit of work: a tile of 128 weight rows x 256 k (16 KB of packed codes).
 // Schedule: stream-K over (tile, 256-k unit), one contiguous range per CTA;
 // tiles split across CTAs are reduced through the workspace by the CTA whose
@@ -17,10 +29,13 @@
 // Warp roles (448 or 320 threads):
 //   warps 0, 1   producers, alternate units.  Lane 0 arms the stage's
 //                mbarrier and issues the packed-W box (TMA, 128 rows x 128 B,
-//                128-byte swizzle) and the unit's X tile (one linear bulk copy
-//                of the image k_xprep wrote, layout 2 / 3); all 32 lanes copy
-//                the unit's scale bytes with 4-byte cp.async and arrive on the
-//                same mbarrier when their copies land.  No multicast.
+//                128-byte swizzle) and the unit's X image with its row
+//                factors (one bulk copy); all 32 lanes copy the unit's scale
+//                bytes, one 8-byte (MXFP4) or 16-byte (NVFP4) cp.async per
+//                weight row, and arrive on the same mbarrier when they land.
+//                Weights and scales do not depend on the preparation grid, so
+//                the first stages' weights go out before the
+//                programmatic-launch wait.  No multicast.
 //   warps 2..    consumers, in unit groups (GtCfg): unit i of the CTA's range
 //                goes to group i % UG, whose warps each own 16 RPW weight rows
 //                and all 256 k of it and run chunk_mma on codes, scales and X
@@ -28,6 +43,10 @@
 //                warps (32 rows each); M <= 16: one group of eight (16 rows).
 //                At each segment end the groups' sums are added in group
 //                order and group 0 stores the tile or its stream-K partial.
+// Every CTA signals its dependents right after its prologue, so the next
+// call's kernels are launched while this one runs and start as its CTAs
+// finish; they read nothing this grid writes before their own
+// programmatic-launch wait returns.
 // Every mbarrier wait is bounded (tc.cuh); on timeout the kernel sets
 // g_gemv_tma_fault and returns after letting copies in flight land.
 #include <cuda.h>
@@ -61,8 +80,12 @@ struct GtCfg {
   static constexpr int SB = (FMT == 0) ? kGtUnitK / 32 : kGtUnitK / 16;   // scale bytes per row per unit
   static constexpr int W_BYTES = kGtRows * kGtUnitK / 2;                // 16 KB
   static constexpr int X_BYTES = MPAD * kGtUnitK * 2;
+  static constexpr int XF_BYTES = 128;                                  // MPAD row factors 2^s (float)
   static constexpr int S_BYTES = kGtRows * SB;
-  static constexpr int STAGE = ((W_BYTES + X_BYTES + S_BYTES) + 1023) / 1024 * 1024;
+  static constexpr int STAGE = ((W_BYTES + X_BYTES + XF_BYTES + S_BYTES) + 1023) / 1024 * 1024;
+  // the W box lands on a 1024-byte boundary (128-byte swizzle); the unit's X
+  // image and its row factors are one bulk copy into [X | XF]
+  static_assert(W_BYTES % 1024 == 0 && XF_BYTES >= 4 * MPAD, "stage layout");
   static constexpr int PART_BYTES = (UG - 1) * kGtGroups * NT * 32 * 16;  // other groups' sums
   static constexpr int STAGES = ((200 * 1024 - PART_BYTES) / STAGE) & ~1;  // even: two producers
   static constexpr int BYTES = 1024 + STAGES * STAGE + 2 * STAGES * 8 + 16 + PART_BYTES;
@@ -72,8 +95,7 @@ struct GtCfg {
 
 struct GtArgs {
   const uint8_t* scales;
-  const uint8_t* xg;     // X in layout 2 of k_xprep: [K/256][mpad][32 chunks], chunk c at (c & ~7) | ((c ^ m) & 7)
-  const float* xs;
+  const uint8_t* xg;     // k_xprep_units image: per 256-k unit, mpad rows x 512 B then mpad row factors
   void* Y;
   float* partials;       // [2 * G][8 row groups][NT][32 lanes] float4
   unsigned* counters;    // [tiles]
@@ -85,6 +107,53 @@ struct GtArgs {
   TpOut tp;              // world > 0: store into every rank's Y_full, then tp_finish
 };
 
+// ---------------------------------------------------------------------------
+// X preparation: one warp per (activation row m < mpad, 256-k unit u).  Lane
+// l converts k = 256 u + 8 l .. + 7 of row m; s from the warp's largest |x|
+// (bf16 bits without the sign are ordered like the magnitudes; an infinity
+// or NaN leaves the row unscaled, so it reaches the output as the
+// reference's non-finite sums do).  Image of unit u at u * (mpad 512 + 128):
+// row m's 16-byte chunk c at m 512 + 16 xg_pos(c, m), then the mpad factors
+// 2^s (rows >= M: zeros and factor 0).
+// ---------------------------------------------------------------------------
+constexpr int kXuWarps = 8;
+__global__ void __launch_bounds__(kXuWarps * 32) k_xprep_units(const uint16_t* __restrict__ X, int M, int K, int mpad,
+                                                              int fmt, uint8_t* __restrict__ img) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // X may be the previous grid's output
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * kXuWarps + (threadIdx.x >> 5);
+  const int KS = K / kGtUnitK;
+  if (gw >= mpad * KS) return;
+  const int u = gw / mpad, m = gw % mpad;
+  uint8_t* unit = img + (size_t)u * (mpad * (kGtUnitK * 2) + 128);
+  uint4 o4 = make_uint4(0u, 0u, 0u, 0u);
+  float f = 0.0f;
+  if (m < M) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(X + (size_t)m * K + (size_t)u * kGtUnitK + 8 * lane));
+    const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+    uint32_t mx = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) mx = max(mx, max(w4[q] & 0x7FFFu, (w4[q] >> 16) & 0x7FFFu));
+    mx = __reduce_max_sync(0xFFFFFFFFu, mx);
+    int sc = 0;  // zero, infinite or NaN: unscaled
+    if (mx != 0 && mx < 0x7F80u) {
+      const int eb = (int)(mx >> 7);
+      const int lg = eb != 0 ? eb - 127 : (31 - __clz((int)mx)) - 133;  // ilogb of the largest |x|
+      sc = lg - 14;
+      sc = sc < -126 ? -126 : (sc > 114 ? 114 : sc);
+    }
+    const float inv = u2f((uint32_t)(127 - sc) << 23);  // 2^-s
+    __half2 o[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) o[q] = __floats2half2_rn(u2f(w4[q] << 16) * inv, u2f(w4[q] & 0xFFFF0000u) * inv);
+    o4 = *reinterpret_cast<const uint4*>(o);
+    f = u2f((uint32_t)(127 + sc) << 23);  // 2^s
+  }
+  *reinterpret_cast<uint4*>(unit + m * (kGtUnitK * 2) + xg_pos(fmt, lane, m) * 16) = o4;
+  if (lane == 0) reinterpret_cast<float*>(unit + mpad * (kGtUnitK * 2))[m] = f;
+}
+
 template <int FMT, int NT, int RPW, int UG, bool F32OUT>
 __global__ void __launch_bounds__(GtCfg<FMT, NT, RPW, UG>::THREADS, 1)
 k_gemv_tma(const __grid_constant__ CUtensorMap map_w, const GtArgs a) {
@@ -95,10 +164,11 @@ k_gemv_tma(const __grid_constant__ CUtensorMap map_w, const GtArgs a) {
   const uint32_t raw = su32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw);
-  // stage s: [W 128 x 128 B (swizzled) | X mpad x 512 B | scales 128 x SB]
+  // stage s: [W 128 x 128 B (swizzled) | X mpad x 512 B | mpad row factors | scales 128 x SB]
   auto W_off = [&](int s) { return s * C::STAGE; };
   auto X_off = [&](int s) { return s * C::STAGE + C::W_BYTES; };
-  auto S_off = [&](int s) { return s * C::STAGE + C::W_BYTES + C::X_BYTES; };
+  auto XF_off = [&](int s) { return s * C::STAGE + C::W_BYTES + C::X_BYTES; };
+  auto S_off = [&](int s) { return s * C::STAGE + C::W_BYTES + C::X_BYTES + C::XF_BYTES; };
   uint64_t* bars = reinterpret_cast<uint64_t*>(gbase + S * C::STAGE);
   auto full_bar = [&](int s) { return su32(&bars[s]); };
   auto empty_bar = [&](int s) { return su32(&bars[S + s]); };
@@ -114,12 +184,13 @@ k_gemv_tma(const __grid_constant__ CUtensorMap map_w, const GtArgs a) {
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(full_bar(s), 1 + 32);   // lane 0's expect_tx arrival + 32 cp.async arrivals
+      mbar_init(full_bar(s), 1 + 32);   // lane 0's expect_tx arrival (W and X) + 32 cp.async arrivals (scales)
       mbar_init(empty_bar(s), C::WPG);  // the unit's group
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   bool ok = true;
 
   if (warp < kGtProd) {
@@ -133,42 +204,44 @@ k_gemv_tma(const __grid_constant__ CUtensorMap map_w, const GtArgs a) {
       p_ks += kGtProd;
       while (p_ks >= KS) { p_ks -= KS; ++p_tile; }
     };
-    auto issue_w = [&](int s) {
-      mbar_expect_tx(full_bar(s), (uint32_t)(C::W_BYTES + C::X_BYTES));
+    auto issue_w = [&](int s) {  // lane 0: the unit's packed-W box; its X follows on the same barrier
+      mbar_expect_tx(full_bar(s), (uint32_t)(C::W_BYTES + C::X_BYTES + C::XF_BYTES));
       tma_load_2d(base + (uint32_t)W_off(s), &map_w, p_ks * (kGtUnitK / 2), p_tile * kGtRows, full_bar(s));
     };
-    auto issue_x = [&](int s, int ks) {
-      const uint8_t* src = a.xg + (size_t)ks * C::X_BYTES;
+    auto issue_x = [&](int s, int ks) {  // lane 0: the unit's f16 X image and row factors (k_xprep_units)
+      const uint8_t* src = a.xg + (size_t)ks * (C::X_BYTES + C::XF_BYTES);
       asm volatile(
           "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-          ::"r"(base + (uint32_t)X_off(s)), "l"(src), "r"((uint32_t)C::X_BYTES), "r"(full_bar(s))
+          ::"r"(base + (uint32_t)X_off(s)), "l"(src), "r"((uint32_t)(C::X_BYTES + C::XF_BYTES)), "r"(full_bar(s))
           : "memory");
     };
+    // all lanes: the unit's scale bytes, one 8-byte (MXFP4) or 16-byte (NVFP4)
+    // copy per weight row, rows lane + 32 q
     auto issue_scales = [&](int s) {
-      constexpr int WPR = C::SB / 4;  // 4-byte words per row
 #pragma unroll
-      for (int e = lane; e < kGtRows * WPR; e += 32) {
-        const int row = e / WPR, wi = e % WPR;
+      for (int q = 0; q < kGtRows / 32; ++q) {
+        const int row = lane + 32 * q;
         int n = p_tile * kGtRows + row;
         n = n < a.N ? n : a.N - 1;  // rows past N: TMA zero-fills their codes
-        const uint8_t* src = a.scales + (size_t)n * srow + (size_t)p_ks * C::SB + 4 * wi;
-        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(base + (uint32_t)(S_off(s) + row * C::SB + 4 * wi)),
-                     "l"(src) : "memory");
+        const uint8_t* src = a.scales + (size_t)n * srow + (size_t)p_ks * C::SB;
+        const uint32_t dst = base + (uint32_t)(S_off(s) + row * C::SB);
+        if (FMT == 0) asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+        else asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
       }
       asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(full_bar(s)) : "memory");
     };
+    if (lane == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_w)) : "memory");
     const int pre = niter < S ? niter : S;
-    // Weights and scales do not depend on the X-preparation grid: start them
-    // first; the first stages' X copies follow once that grid is done.
+    // Weights and scales do not depend on the previous grid: the first stages'
+    // go out before the programmatic-launch wait; X follows it.
     for (int i = p; i < pre; i += kGtProd) {
       if (lane == 0) issue_w(i % S);
       issue_scales(i % S);
       advance();
     }
-    if (lane == 0) {
-      asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // the X image is the preparation grid's output
+    if (lane == 0)
       for (int i = p; i < pre; i += kGtProd) issue_x(i % S, (int)((it0 + i) % KS));
-    }
     for (int i = pre + ((p - pre % kGtProd + kGtProd) % kGtProd); i < niter; i += kGtProd) {
       const int s = i % S;
       if (lane == 0) ok = mbar_wait_flag(empty_bar(s), ((i / S) + 1) & 1, fault);
@@ -186,9 +259,11 @@ k_gemv_tma(const __grid_constant__ CUtensorMap map_w, const GtArgs a) {
     const int wq = cons % WPG;                      // weight rows [16 RPW wq, 16 RPW (wq + 1)) of a unit
     const int g = lane >> 2, j = lane & 3;
     const uint32_t sw = (uint32_t)(g & 7);         // every row this lane touches is g mod 8
-    asm volatile("griddepcontrol.wait;" ::: "memory");  // xs written by the X-preparation grid
+    // (no programmatic-launch wait here: every consumer step depends on a
+    // unit whose X the producers copied after theirs)
 
-    float acc[RPW][NT][4];
+    float acc[RPW][NT][4];   // FP32 sums in absolute scale
+    float accu[RPW][NT][4];  // one unit's sums, in that unit's X scale
     auto zero = [&](float (&v)[RPW][NT][4]) {
 #pragma unroll
       for (int r = 0; r < RPW; ++r)
@@ -212,7 +287,7 @@ k_gemv_tma(const __grid_constant__ CUtensorMap map_w, const GtArgs a) {
             const int n = tile * kGtRows + 16 * grp(r) + g + ((e & 2) ? 8 : 0);
             const int m = 8 * t + 2 * j + (e & 1);
             if (n < a.N && m < a.M) {
-              float y = v[r][t][e] * __ldg(a.xs + m);
+              float y = v[r][t][e];
               if (FMT == 1) y *= a.ts;
               if (F32OUT) static_cast<float*>(a.Y)[(size_t)m * a.ldy + n] = y;
               else if (a.tp.world > 0) tp_store(a.tp, (size_t)m, n, __float2bfloat16_rn(y));
@@ -245,14 +320,32 @@ k_gemv_tma(const __grid_constant__ CUtensorMap map_w, const GtArgs a) {
         __threadfence();
         float sum[RPW][NT][4];
         zero(sum);
-        for (int cc = c_lo; cc <= c_hi; ++cc) {
-          const float4* src = reinterpret_cast<const float4*>(a.partials) + (size_t)slot_of(cc, tile) * kGtGroups * NT * 32;
+        // CB contributors' partials in flight before the first add (they come
+        // from L2); the adds stay in CTA order
+        constexpr int CB = 2;
+#pragma unroll 1
+        for (int cb = c_lo; cb <= c_hi; cb += CB) {
+          float4 pv[CB][RPW][NT];
 #pragma unroll
-          for (int r = 0; r < RPW; ++r)
+          for (int u = 0; u < CB; ++u)
+            if (cb + u <= c_hi) {
+              const float4* src =
+                  reinterpret_cast<const float4*>(a.partials) + (size_t)slot_of(cb + u, tile) * kGtGroups * NT * 32;
 #pragma unroll
-            for (int t = 0; t < NT; ++t) {
-              const float4 pv = __ldcg(src + (grp(r) * NT + t) * 32 + lane);
-              sum[r][t][0] += pv.x; sum[r][t][1] += pv.y; sum[r][t][2] += pv.z; sum[r][t][3] += pv.w;
+              for (int r = 0; r < RPW; ++r)
+#pragma unroll
+                for (int t = 0; t < NT; ++t) pv[u][r][t] = __ldcg(src + (grp(r) * NT + t) * 32 + lane);
+            }
+#pragma unroll
+          for (int u = 0; u < CB; ++u)
+            if (cb + u <= c_hi) {
+#pragma unroll
+              for (int r = 0; r < RPW; ++r)
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                  sum[r][t][0] += pv[u][r][t].x; sum[r][t][1] += pv[u][r][t].y;
+                  sum[r][t][2] += pv[u][r][t].z; sum[r][t][3] += pv[u][r][t].w;
+                }
             }
         }
         store(tile, sum);
@@ -274,6 +367,7 @@ k_gemv_tma(const __grid_constant__ CUtensorMap map_w, const GtArgs a) {
           const uint8_t* W = gbase + W_off(s);
           const uint8_t* X = gbase + X_off(s);
           const uint8_t* SC = gbase + S_off(s);
+          zero(accu);
 #pragma unroll
           for (int c = 0; c < 2; ++c) {  // the unit's two 128-k chunks
             uint32_t cw[RPW][2][4], cs[RPW][2], cx[NT][16];
@@ -305,7 +399,20 @@ k_gemv_tma(const __grid_constant__ CUtensorMap map_w, const GtArgs a) {
                 cx[t][4 * q] = v.x; cx[t][4 * q + 1] = v.y; cx[t][4 * q + 2] = v.z; cx[t][4 * q + 3] = v.w;
               }
             }
-            chunk_mma<FMT, RPW, NT>(acc, cw, cs, cx);
+            chunk_mma<FMT, RPW, NT>(accu, cw, cs, cx);
+          }
+          // acc += unit sums * 2^s of their activation rows (exact scaling)
+          const float* XF = reinterpret_cast<const float*>(gbase + XF_off(s));
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+            const float2 xf = *reinterpret_cast<const float2*>(XF + 8 * t + 2 * j);
+#pragma unroll
+            for (int r = 0; r < RPW; ++r) {
+              acc[r][t][0] = fmaf(accu[r][t][0], xf.x, acc[r][t][0]);
+              acc[r][t][1] = fmaf(accu[r][t][1], xf.y, acc[r][t][1]);
+              acc[r][t][2] = fmaf(accu[r][t][2], xf.x, acc[r][t][2]);
+              acc[r][t][3] = fmaf(accu[r][t][3], xf.y, acc[r][t][3]);
+            }
           }
         }
         __syncwarp();
@@ -359,16 +466,20 @@ k_gemv_tma(const __grid_constant__ CUtensorMap map_w, const GtArgs a) {
 bool make_tma_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr, uint64_t inner, uint64_t outer,
                      uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw);
 
+// Each weight row's scales of a unit are copied as one 8-byte (MXFP4) or
+// 16-byte (NVFP4) piece: the scale array must start on such a boundary (the
+// row pitch K / 32 or K / 16 is a multiple of it since K % 256 == 0).
 bool gemv_tma_supported(const qgemm_weights_t* w, int mb) {
+  const uintptr_t salign = w->format == QGEMM_FMT_MXFP4 ? 7u : 15u;
   return mb >= 1 && mb <= 16 && (w->format == QGEMM_FMT_MXFP4 || w->format == QGEMM_FMT_NVFP4) &&
          w->K % kGtUnitK == 0 && w->K <= (size_t)INT32_MAX / 2 && w->N <= (size_t)INT32_MAX / 2 &&
-         (reinterpret_cast<uintptr_t>(w->scales) & 3u) == 0;
+         (reinterpret_cast<uintptr_t>(w->scales) & salign) == 0;
 }
 
 struct GtPlan {
   int nt, mpad, tiles, KS, G;
   long long T;
-  size_t counter_bytes, partial_bytes, xg_bytes;
+  size_t counter_bytes, partial_bytes, image_bytes;
 };
 static GtPlan gt_plan(const qgemm_weights_t* w, int mb, int sm_count) {
   GtPlan p;
@@ -380,13 +491,13 @@ static GtPlan gt_plan(const qgemm_weights_t* w, int mb, int sm_count) {
   p.G = (int)(p.T < sm_count ? p.T : sm_count);
   p.counter_bytes = ((size_t)p.tiles * sizeof(unsigned) + 255) & ~(size_t)255;
   p.partial_bytes = (((size_t)2 * p.G * kGtGroups * p.nt * 32 * sizeof(float4)) + 255) & ~(size_t)255;
-  p.xg_bytes = (((size_t)16 * w->K * 2) + 255) & ~(size_t)255;  // room for mpad = 16
+  p.image_bytes = (((size_t)p.KS * (p.mpad * kGtUnitK * 2 + 128)) + 255) & ~(size_t)255;
   return p;
 }
-// [counters | partials | X image (16 rows)]; xs lives with the caller's layout
+// [counters | partials | X image], sized for 16 activation rows (two n-tiles)
 size_t gemv_tma_workspace(const qgemm_weights_t* w, int sm_count) {
   const GtPlan p = gt_plan(w, 16, sm_count);
-  return p.counter_bytes + p.partial_bytes + p.xg_bytes;
+  return p.counter_bytes + p.partial_bytes + p.image_bytes;
 }
 
 // Consumer layout per activation-tile count: M <= 8, three unit groups of
@@ -425,11 +536,11 @@ static cudaError_t launch_gt_t(const CUtensorMap& mw, const GtArgs& a, cudaStrea
   return cudaLaunchKernelEx(&cfg, k_gemv_tma<FMT, NT, gt_rpw<NT>(), gt_ug<NT>(), F32>, mw, a);
 }
 
-// One launch over mb <= 16 activation rows whose X image (layout 2 of
-// k_xprep, mpad = 8 * ceil(mb / 8)) and row factors are already in xg / xs.
+// Two launches over mb <= 16 activation rows X (bf16 [mb][K], 16-byte
+// aligned): k_xprep_units, then the GEMM (programmatic dependent launch).
 // ws: gemv_tma_workspace bytes, counters zero.
-qgemm_status_t gemm_gemv_tma(const qgemm_weights_t* w, const __half* xg, const float* xs, int mb, void* Y, int ldy,
-                             bool f32, void* ws, int sm_count, cudaStream_t s, const TpOut* tp) {
+qgemm_status_t gemm_gemv_tma(const qgemm_weights_t* w, const uint16_t* X, int mb, void* Y, int ldy, bool f32,
+                             void* ws, int sm_count, cudaStream_t s, const TpOut* tp) {
   if (!gemv_tma_supported(w, mb)) return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "TMA decode path: unsupported shape");
   if (sm_count <= 0) return fail(QGEMM_ERR_CUDA, "TMA decode path: no device properties");
   const GtPlan p = gt_plan(w, mb, sm_count);
@@ -437,10 +548,24 @@ qgemm_status_t gemm_gemv_tma(const qgemm_weights_t* w, const __half* xg, const f
   if (!make_tma_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->data, w->K / 2, w->N, w->K / 2, kGtUnitK / 2, kGtRows,
                        CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(QGEMM_ERR_CUDA, "TMA decode path: cuTensorMapEncodeTiled failed");
+  uint8_t* img = static_cast<uint8_t*>(ws) + p.counter_bytes + p.partial_bytes;
+  {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((p.mpad * p.KS + kXuWarps - 1) / kXuWarps));
+    cfg.blockDim = dim3(kXuWarps * 32);
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, k_xprep_units, X, mb, (int)w->K, p.mpad,
+                                             w->format == QGEMM_FMT_MXFP4 ? 0 : 1, img);
+    if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "TMA decode X preparation: %s", cudaGetErrorString(e));
+  }
   GtArgs a;
   a.scales = static_cast<const uint8_t*>(w->scales);
-  a.xg = reinterpret_cast<const uint8_t*>(xg);
-  a.xs = xs;
+  a.xg = img;
   a.Y = Y;
   a.counters = static_cast<unsigned*>(ws);
   a.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + p.counter_bytes);
@@ -461,11 +586,6 @@ qgemm_status_t gemm_gemv_tma(const qgemm_weights_t* w, const __half* xg, const f
   }
   if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "TMA decode launch: %s", cudaGetErrorString(e));
   return QGEMM_OK;
-}
-
-size_t gemv_tma_xg_offset(const qgemm_weights_t* w, int sm_count) {
-  const GtPlan p = gt_plan(w, 16, sm_count);
-  return p.counter_bytes + p.partial_bytes;
 }
 
 cudaError_t gemv_tma_fault_clear() {
