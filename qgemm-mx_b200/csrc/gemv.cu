@@ -143,8 +143,10 @@ __device__ __forceinline__ float absmax8(const uint4 v, float a) {
 __global__ void __launch_bounds__(kXpThreads) k_xprep(const uint16_t* __restrict__ X, int M, int K, int perm,
                                                       int layout, int lp, __half* __restrict__ Xh,
                                                       float* __restrict__ xs) {
+  // Dependents may launch at once (this grid is resident when the trigger
+  // fires); they read nothing written here before their own wait returns.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;");
   const int m = blockIdx.x;
   constexpr int kStride = kXpThreads * 8;
   if (m >= M) {  // zero padding rows of the last activation block
@@ -221,6 +223,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) k_gemv(const GemvArgs a) {
   const int M = a.M, N = a.N, K = a.K, C = a.C;
   const size_t rowb = (size_t)K / 2;
   const bool active = w < a.W_total;
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the next call's kernels may launch
   const long long start = active ? (long long)w * a.T / a.W_total : 0;
   const long long end = active ? (long long)(w + 1) * a.T / a.W_total : 0;
 

@@ -119,8 +119,10 @@ struct GtArgs {
 constexpr int kXuWarps = 8;
 __global__ void __launch_bounds__(kXuWarps * 32) k_xprep_units(const uint16_t* __restrict__ X, int M, int K, int mpad,
                                                               int fmt, uint8_t* __restrict__ img) {
-  asm volatile("griddepcontrol.wait;" ::: "memory");  // X may be the previous grid's output
+  // Dependents (the GEMM) may launch at once and stream their weights; they
+  // read the image only after their own wait, which covers this grid.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // X may be the previous grid's output
   const int lane = threadIdx.x & 31;
   const int gw = blockIdx.x * kXuWarps + (threadIdx.x >> 5);
   const int KS = K / kGtUnitK;

@@ -116,6 +116,9 @@ k_umma_ts(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUt
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // the next call's kernels may launch now; they take SMs as this grid's
+  // CTAs finish and read nothing it writes before their own wait returns
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const uint32_t tmem_a = tmem + (uint32_t)BN;
   bool ok = true;
 

@@ -144,8 +144,10 @@ __device__ __forceinline__ float2 e4m3x2_f32(uint32_t v) {  // low byte -> .x
 }
 __global__ void __launch_bounds__(256) k_xprep_bs(const uint16_t* __restrict__ X, int M, int K, int BN, int nrows,
                                                   uint8_t* __restrict__ img) {
+  // Dependents (the GEMM) may launch at once and stream their weights; they
+  // read the image only after their own wait, which covers this grid.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;");
   const int KS = K / kBsK;
   const long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -256,6 +258,9 @@ k_umma_bs(const __grid_constant__ CUtensorMap map_w, const BsArgs a) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // the next call's kernels may launch now; they take SMs as this grid's
+  // CTAs finish and read nothing it writes before their own wait returns
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   bool ok = true;
 
   if (warp < kBsWProds) {
