@@ -75,6 +75,8 @@ def parse():
     ap.add_argument("--prefill", action="store_true",
                     help="compute-bound table: NVFP4 (28672,8192) and (8192,28672), M in {2048,4096,8192}, "
                          "tcgen05 path vs cuBLAS BF16 of the same shape")
+    ap.add_argument("--moe", default=None, choices=sorted(MOE_STEPS),
+                    help="mixture-of-experts decode step: one grouped call vs one call per active expert")
     ap.add_argument("--case", default=None,
                     help="fmt,N,K,M: run only that GEMM --steps times (for profilers), print its mean time")
     return ap.parse_args()
@@ -112,6 +114,87 @@ def run_case(args):
     qg.lib().qgemm_umma_status(C.byref(f))  # nonzero: a bounded wait gave up (times and outputs invalid)
     print(json.dumps({"case": args.case, "us_per_call": round(us, 3), "gbs": round(nb / us / 1e3, 1),
                       "wait_timed_out": bool(f.value)}))
+
+
+# Mixture-of-experts decode steps (expert gate-up projections, MXFP4):
+# (experts, N, K, experts per token, tokens).  Shapes of DeepSeek-V3-class
+# (256 experts, 2 x 2048 x 7168) and Mixtral-8x7B-class (8 experts,
+# 2 x 14336 x 4096) models; random weights, seeded skewed routing.
+MOE_STEPS = {
+    "deepseek_v3_gate_up": (256, 4096, 7168, 8, 32),
+    "mixtral_gate_up": (8, 28672, 4096, 2, 16),
+}
+
+
+def moe_routing(E, topk, tokens, seed=0):
+    """Per-expert row counts of one step: every token picks topk distinct
+    experts with probability proportional to 1 / (rank + 1) ** 1.1 over a
+    shuffled expert order (a skewed, Zipf-like popularity)."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    pop = 1.0 / (np.arange(E) + 1.0) ** 1.1
+    pop = pop[rng.permutation(E)]
+    pop /= pop.sum()
+    counts = np.zeros(E, np.int64)
+    for _ in range(tokens):
+        counts[rng.choice(E, topk, replace=False, p=pop)] += 1
+    return [int(c) for c in counts]
+
+
+def run_moe(args):
+    """One MoE decode step's expert GEMMs: qgemm_grouped_gemm_w4a16 (decode-
+    sized experts fused 32 per launch) against one qgemm_gemm_w4a16 per active
+    expert, both captured as CUDA graphs and replayed (CUDA events, median);
+    the active experts' weights exceed L2, so every replay reads them from
+    HBM."""
+    import torch
+    qg = importlib.import_module("qgemm-mx_b200")
+    E, N, K, topk, tokens = MOE_STEPS[args.moe]
+    counts = moe_routing(E, topk, tokens)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(5)
+    experts = []
+    for _ in range(E):
+        W = torch.randn((N, K), generator=gen, device="cuda").mul_(0.02)
+        experts.append(qg.pack_mxfp4(W))
+        del W
+    torch.cuda.empty_cache()
+    rows = sum(counts)
+    offs = [sum(counts[:e]) for e in range(E)]
+    X = torch.randn((rows, K), generator=gen, device="cuda").to(torch.bfloat16)
+    Yg = torch.zeros((rows, N), dtype=torch.bfloat16, device="cuda")
+    Yl = torch.zeros_like(Yg)
+    active = [e for e in range(E) if counts[e]]
+    wsg = qg.make_grouped_workspace(experts, max(counts))
+    wsl = torch.zeros(max(qg.workspace_size(experts[e], counts[e]) for e in active), dtype=torch.uint8,
+                      device="cuda")
+    stream = torch.cuda.Stream()
+
+    def grouped(_):
+        qg.grouped_gemm_w4a16(experts, X, counts, offsets=offs, out=Yg, workspace=wsg)
+
+    def loop(_):
+        for e in active:
+            o, m = offs[e], counts[e]
+            qg.gemm_w4a16(experts[e], X[o:o + m], out=Yl[o:o + m], workspace=wsl)
+
+    us_g = time_graphed(grouped, 4, stream)
+    us_l = time_graphed(loop, 4, stream)
+    torch.cuda.synchronize()
+    diff = float(((Yg.float() - Yl.float()).norm() / Yl.float().norm().clamp_min(1e-30)).item())
+    nbytes = sum(qg.total_bytes(qg.MXFP4, counts[e], N, K) for e in active)
+    fused = sum(1 for e in active if counts[e] <= 16)
+    launches_g = 2 * ((fused + 31) // 32) + sum(qg.launch_count(experts[e], counts[e])[0]
+                                                for e in active if counts[e] > 16)
+    launches_l = sum(qg.launch_count(experts[e], counts[e])[0] for e in active)
+    print(json.dumps({
+        "moe": args.moe, "experts": E, "N": N, "K": K, "topk": topk, "tokens": tokens,
+        "active_experts": len(active), "max_rows": max(counts), "rows": rows,
+        "grouped_us": round(us_g, 2), "per_expert_calls_us": round(us_l, 2),
+        "speedup": round(us_l / us_g, 3),
+        "grouped_gbs": round(nbytes / us_g / 1e3, 1), "per_expert_calls_gbs": round(nbytes / us_l / 1e3, 1),
+        "launches_grouped": launches_g, "launches_per_expert_calls": launches_l,
+        "rel_frobenius_grouped_vs_calls": diff}))
 
 
 def run_prefill(args):
@@ -551,6 +634,9 @@ def main():
         return
     if args.prefill:
         run_prefill(args)
+        return
+    if args.moe:
+        run_moe(args)
         return
     if args.impl == "reference":
         run_reference_arm(args)

@@ -113,10 +113,14 @@ qgemm_status_t qgemm_codec_encode(int32_t kind, const float* in, void* out,
                                   size_t n, void* stream);
 
 /* ---- GEMM ------------------------------------------------------------------
- * Workspace: scratch the kernels use for split-K partial sums and tile
- * counters.  Size it with qgemm_workspace_size(); zero it once before first
- * use (qgemm_workspace_init or cudaMemsetAsync).  Every call leaves it zeroed
- * again.  Calls that may overlap on the GPU need distinct workspaces.        */
+ * Workspace: scratch the kernels use for split-K partial sums, tile tickets
+ * and the converted copy of X.  Size it with qgemm_workspace_size(); zero it
+ * once before first use (qgemm_workspace_init or cudaMemsetAsync).  The
+ * tickets sit at the start of every workspace in a region sized from N, and
+ * every call returns them to zero, so one workspace of at least
+ * qgemm_workspace_size(w, M) bytes for each M it meets (the size is not
+ * monotone in M: the kernel changes) serves all those calls in stream order.
+ * Calls that may overlap on the GPU need distinct workspaces.                */
 size_t qgemm_workspace_size(const qgemm_weights_t* w, int32_t M);
 qgemm_status_t qgemm_workspace_init(void* workspace, size_t ws_bytes, void* stream);
 /* Number of kernel launches one qgemm_gemm_w4a16 call makes for (w, M), and
@@ -137,6 +141,28 @@ qgemm_status_t qgemm_gemm_w4a16(const qgemm_weights_t* w, const uint16_t* X,
 qgemm_status_t qgemm_gemm_w4a16_f32(const qgemm_weights_t* w, const uint16_t* X,
                                     int32_t M, float* Y, void* workspace,
                                     size_t ws_bytes, void* stream);
+
+/* ---- grouped GEMM (mixture of experts) ------------------------------------
+ * E weight sets w[0 .. E-1] of one format and shape (N, K).  Expert e
+ * multiplies its M[e] activation rows, rows offs[e] .. offs[e] + M[e] - 1 of
+ * X (bf16 bits [rows][K]), and writes the same rows of Y (bf16 bits
+ * [rows][N]):  Y[offs[e] + i] = X[offs[e] + i] . W_e^T,  0 <= i < M[e].
+ * M[e] = 0 skips expert e.  M and offs are host arrays: the routing counts
+ * are on the host when the call is made.  The reference plans this as its
+ * grouped / MoE variant with variable M per expert
+ * (docs/PROJECT-v2.0-fp4-hopper.md:89-90, MASTER_EXECUTION_PLAN.md:249) and
+ * does not build it; each expert's result is a qgemm_gemm_w4a16 result
+ * (same bounds against ref_gemm.hpp:15-27).  MXFP4 / NVFP4 experts with
+ * 1 <= M[e] <= 16 run up to 32 at a time as one X-preparation launch and one
+ * decode-GEMM launch whose stream-K iteration space covers all of them;
+ * other experts run as qgemm_gemm_w4a16 calls on the same stream.
+ * workspace: qgemm_grouped_workspace_size(w, E, max_m) bytes serve every call
+ * whose M[e] <= max_m; zero it once (qgemm_workspace_init).  A workspace
+ * sized for both also serves qgemm_gemm_w4a16 calls. */
+size_t qgemm_grouped_workspace_size(const qgemm_weights_t* w, int32_t E, int32_t max_m);
+qgemm_status_t qgemm_grouped_gemm_w4a16(const qgemm_weights_t* w, int32_t E, const uint16_t* X,
+                                        const int32_t* M, const int64_t* offs, uint16_t* Y,
+                                        void* workspace, size_t ws_bytes, void* stream);
 
 /* ---- tensor parallel over the GPUs of one node (W sharded along N) -------
  * No counterpart in the reference, which runs on one GPU; the sharding

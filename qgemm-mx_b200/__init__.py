@@ -73,6 +73,9 @@ _sig("qgemm_workspace_init", _i32, [_vp, _sz, _vp])
 _sig("qgemm_gemm_w4a16", _i32, [C.POINTER(_Weights), _vp, _i32, _vp, _vp, _sz, _vp])
 _sig("qgemm_gemm_w4a16_f32", _i32, [C.POINTER(_Weights), _vp, _i32, _vp, _vp, _sz, _vp])
 _sig("qgemm_gemm_w4a16_noalloc", _i32, [C.POINTER(_Weights), _vp, _i32, _vp, _vp])
+_sig("qgemm_grouped_workspace_size", _sz, [C.POINTER(_Weights), _i32, _i32])
+_sig("qgemm_grouped_gemm_w4a16", _i32, [C.POINTER(_Weights), _i32, _vp, C.POINTER(_i32), C.POINTER(C.c_int64),
+                                        _vp, _vp, _sz, _vp])
 _sig("qgemm_cublas_bf16_gemm", _i32, [_vp, _vp, _i32, _sz, _sz, _vp, _vp])
 _sig("qgemm_probe_launch", _i32, [_i32, _vp, _vp, _sz, _vp])
 _sig("qgemm_cublaslt_fp8_gemm", _i32, [_vp, _vp, _i32, _sz, _sz, _vp, _vp, _vp, _vp, _sz, _vp])
@@ -327,6 +330,62 @@ def gemm_w4a16(p: Packed, X: torch.Tensor, out: torch.Tensor | None = None,
     fn = _lib.qgemm_gemm_w4a16_f32 if out.dtype == torch.float32 else _lib.qgemm_gemm_w4a16
     _check(fn(C.byref(d), _ptr(X), M, _ptr(out), _ptr(workspace), workspace.numel(), _stream(stream)),
            "gemm_w4a16")
+    return out
+
+
+# ---- grouped GEMM (mixture of experts) ------------------------------------------
+
+def _expert_descs(experts: list[Packed]):
+    return (_Weights * len(experts))(*[p.desc() for p in experts])
+
+
+def grouped_workspace_size(experts: list[Packed], max_m: int) -> int:
+    """Workspace bytes for grouped_gemm_w4a16 calls whose experts have <= max_m rows."""
+    if not experts:
+        return 0
+    return _lib.qgemm_grouped_workspace_size(_expert_descs(experts), len(experts), max_m)
+
+
+def make_grouped_workspace(experts: list[Packed], max_m: int, stream=None) -> torch.Tensor:
+    n = max(grouped_workspace_size(experts, max_m), 256)
+    ws = torch.empty(n, dtype=torch.uint8, device=experts[0].data.device)
+    _check(_lib.qgemm_workspace_init(_ptr(ws), n, _stream(stream)), "workspace_init")
+    return ws
+
+
+def grouped_gemm_w4a16(experts: list[Packed], X: torch.Tensor, counts, offsets=None,
+                       out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+                       stream=None) -> torch.Tensor:
+    """Mixture-of-experts GEMM: rows offsets[e] .. offsets[e] + counts[e] of X
+    (bf16 [rows, K]) go through expert e; Y holds the same rows (bf16 [rows, N]).
+    offsets defaults to the exclusive prefix sum of counts (rows sorted by
+    expert).  Rows no expert covers are left as they are in ``out``."""
+    E = len(experts)
+    counts = [int(c) for c in counts]
+    if len(counts) != E:
+        raise ValueError("grouped_gemm_w4a16: one count per expert")
+    if offsets is None:
+        offsets, acc = [], 0
+        for c in counts:
+            offsets.append(acc)
+            acc += c
+    offsets = [int(o) for o in offsets]
+    if X.dim() != 2 or X.dtype != torch.bfloat16 or (E and X.shape[1] != experts[0].K):
+        raise ValueError("grouped_gemm_w4a16: X must be bf16 [rows, K]")
+    for c, o in zip(counts, offsets):
+        if c > 0 and o + c > X.shape[0]:
+            raise ValueError("grouped_gemm_w4a16: expert rows beyond X")
+    X = X.contiguous()
+    if out is None:
+        out = torch.zeros((X.shape[0], experts[0].N if E else 0), dtype=torch.bfloat16, device=X.device)
+    if E == 0:
+        return out
+    if workspace is None:
+        workspace = make_grouped_workspace(experts, max(max(counts), 1), stream)
+    Ms = (_i32 * E)(*counts)
+    Os = (C.c_int64 * E)(*offsets)
+    _check(_lib.qgemm_grouped_gemm_w4a16(_expert_descs(experts), E, _ptr(X), Ms, Os, _ptr(out), _ptr(workspace),
+                                         workspace.numel(), _stream(stream)), "grouped_gemm_w4a16")
     return out
 
 

@@ -53,6 +53,15 @@ struct DevProps {
 };
 qgemm_status_t device_props(DevProps* p);
 
+// Every GEMM workspace starts with the split-tile tickets of whichever kernel
+// a call runs, in a region sized from N alone: the largest ticket count of
+// any path (the grouped decode kernel's 32 problems x N/128 tiles, the
+// LDG-fed decode kernel's N/32 tiles, at least 512 for the tile-per-CTA
+// tcgen05 kernel's split tiles).  Each call returns its tickets to zero and
+// keeps its other scratch behind the region, so calls of any M, grouped
+// calls included, can share one workspace.
+size_t ws_ticket_bytes(size_t N);
+
 // ---------------------------------------------------------------------------
 // Bit helpers
 // ---------------------------------------------------------------------------

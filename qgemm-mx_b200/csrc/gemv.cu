@@ -91,19 +91,12 @@ struct GemvArgs {
 //     and each 64-k block, BN rows of 128 bytes whose 16-byte chunk c is
 //     stored at chunk c ^ (row % 8) -- the shared-memory image of a
 //     128-byte-swizzled K-major tile, so one linear bulk copy stages it.
-//  2, 3  TMA decode image (lp = mpad rows): for each 256-k unit, mpad rows
-//     of 32 16-byte chunks, chunk c of row m at xg_pos(c, m) (gemv_core.cuh;
-//     2 for MXFP4 and 3 for NVFP4 consumers), so the warp-MMA fragment loads
-//     from shared memory are free of bank conflicts.
+// (The TMA-fed decode kernel has its own preparation, k_xprep_units.)
 // Rows M .. (padded row count) - 1 (one CTA each) are written as zeros.
 __device__ __forceinline__ size_t xprep_index(int m, int k, int K, int layout, int lp) {
   if (layout == 0) return (size_t)m * K + k;
-  if (layout == 1) {
-    const int mb = m / lp, r = m % lp, kb = k >> 6, c = (k >> 3) & 7;
-    return (((size_t)mb * (K >> 6) + kb) * lp + r) * 64 + (size_t)((c ^ (r & 7)) << 3);
-  }
-  const int u = k >> 8, c = (k >> 3) & 31;
-  return (((size_t)u * lp + m) * 32 + xg_pos(layout == 2 ? 0 : 1, c, m)) * 8;
+  const int mb = m / lp, r = m % lp, kb = k >> 6, c = (k >> 3) & 7;
+  return (((size_t)mb * (K >> 6) + kb) * lp + r) * 64 + (size_t)((c ^ (r & 7)) << 3);
 }
 // One pass: every thread issues all its 16-byte loads of the row before it
 // uses any (up to kXpChunks of them, i.e. K <= 256 * 8 * kXpChunks), keeps
@@ -393,16 +386,14 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) k_gemv(const GemvArgs a) {
         for (int t = 0; t < NT; ++t)
           __stcg(mine + ((r * NT + t) * 32 + lane),
                  make_float4(acc[r][t][0], acc[r][t][1], acc[r][t][2], acc[r][t][3]));
-      __threadfence();
-      __syncwarp();
+      __syncwarp();  // the warp's partial stores, then one acquire-release ticket
       const long long t0 = (long long)tile * C, t1 = t0 + C - 1;
       const int w_lo = (int)(((t0 + 1) * a.W_total - 1) / a.T);
       const int w_hi = (int)(((t1 + 1) * a.W_total - 1) / a.T);
       unsigned ticket = 0;
-      if (lane == 0) ticket = atomicAdd(a.counters + tile, 1u);
+      if (lane == 0) ticket = ticket_acq_rel(a.counters + tile);
       ticket = __shfl_sync(0xFFFFFFFFu, ticket, 0);
       if ((int)ticket == w_hi - w_lo) {  // last contributor: reduce in warp order
-        __threadfence();
         float sum[R][NT][4];
 #pragma unroll
         for (int r = 0; r < R; ++r)
@@ -534,6 +525,14 @@ static int occ_for(int nt) { return nt == 1 ? occupancy_of<FMT, 1>() : occupancy
 
 static size_t pad256(size_t b) { return (b + 255) & ~(size_t)255; }
 
+size_t ws_ticket_bytes(size_t N) {
+  size_t n = (N + kTileRows - 1) / kTileRows;
+  const size_t grouped = (size_t)32 * ((N + 127) / 128);
+  if (grouped > n) n = grouped;
+  if (n < 512) n = 512;
+  return pad256(n * sizeof(unsigned));
+}
+
 // Plan for one launch over mb (<= 16) activation rows.
 qgemm_status_t gemv_plan(const qgemm_weights_t* w, int mb, GemvPlan* p) {
   const int f = fmt_code(w->format);
@@ -567,7 +566,7 @@ qgemm_status_t gemv_plan(const qgemm_weights_t* w, int mb, GemvPlan* p) {
   p->W_total = (int)warps;
   p->grid = (int)((warps + kWarpsPerCta - 1) / kWarpsPerCta);
   const size_t slot = (size_t)kRowTiles * p->nt * 4 * 32 * sizeof(float);
-  p->counter_bytes = pad256((size_t)p->tiles * sizeof(unsigned));
+  p->counter_bytes = ws_ticket_bytes(w->N);
   p->partial_bytes = pad256(2 * (size_t)p->W_total * slot);
   p->xs_bytes = pad256((size_t)kMaxM * sizeof(float));
   p->xh_bytes = pad256((size_t)kMaxM * w->K * sizeof(__half));
@@ -631,9 +630,9 @@ static cudaError_t launch_gemv(const GemvPlan& p, const GemvArgs& a, cudaStream_
 static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 qgemm_status_t gemm_umma_ts(const qgemm_weights_t* w, const __half* Xh, const float* xs, int M, void* Y, bool f32,
-                            int splits, void* split_ws, cudaStream_t s);
+                            int splits, unsigned* tickets, void* partials, cudaStream_t s);
 int umma_splits(const qgemm_weights_t* w, int M, int sm_count);
-size_t umma_split_workspace(const qgemm_weights_t* w, int M, int splits);
+size_t umma_split_workspace(const qgemm_weights_t* w, int M, int splits);  // partials only
 
 bool umma_bs_supported(const qgemm_weights_t* w, int M);
 size_t umma_bs_workspace(const qgemm_weights_t* w, int M, int sm_count);
@@ -641,9 +640,9 @@ qgemm_status_t gemm_umma_bs(const qgemm_weights_t* w, const uint16_t* X, int M, 
                             int sm_count, cudaStream_t s, const TpOut* tp);
 bool umma_sk_supported(const qgemm_weights_t* w, int M);
 int umma_sk_bn(int M);
-size_t umma_sk_workspace(const qgemm_weights_t* w, int M, int sm_count);
+size_t umma_sk_workspace(const qgemm_weights_t* w, int M, int sm_count);  // partials only
 qgemm_status_t gemm_umma_sk(const qgemm_weights_t* w, const __half* Xh, const float* xs, int M, void* Y, bool f32,
-                            void* ws, int sm_count, cudaStream_t s, const TpOut* tp);
+                            unsigned* tickets, void* partials, int sm_count, cudaStream_t s, const TpOut* tp);
 
 bool gemv_tma_supported(const qgemm_weights_t* w, int mb);
 size_t gemv_tma_workspace(const qgemm_weights_t* w, int sm_count);
@@ -668,13 +667,13 @@ static int umma_split_count(const qgemm_weights_t* w, int M) {
   const int sms = sm_count_or_zero();
   return sms > 0 ? umma_splits(w, M, sms) : 1;
 }
-// [xs | Xh | split tickets and partials]
+// [tickets | xs | Xh | split partials]
 static size_t umma_xh_bytes(const qgemm_weights_t* w, int M) {
   const int rows = umma_sk_supported(w, M) ? (M + umma_sk_bn(M) - 1) / umma_sk_bn(M) * umma_sk_bn(M) : M;
   return pad256((size_t)rows * w->K * sizeof(__half));
 }
 static size_t umma_workspace(const qgemm_weights_t* w, int M) {
-  const size_t head = pad256((size_t)M * sizeof(float)) + umma_xh_bytes(w, M);
+  const size_t head = ws_ticket_bytes(w->N) + pad256((size_t)M * sizeof(float)) + umma_xh_bytes(w, M);
   if (umma_sk_supported(w, M)) {
     const int sms = sm_count_or_zero();
     return sms > 0 ? head + umma_sk_workspace(w, M, sms) : 0;
@@ -712,17 +711,19 @@ qgemm_status_t gemm_decode_ex(const qgemm_weights_t* w, const uint16_t* X, int M
     if (!ws || !al16(ws) || ws_bytes < need)
       return fail(QGEMM_ERR_WORKSPACE, "gemm: 16-byte aligned workspace of %zu bytes needed, %zu given", need,
                   ws_bytes);
-    float* xs = static_cast<float*>(ws);
-    __half* xh = reinterpret_cast<__half*>(static_cast<uint8_t*>(ws) + pad256((size_t)M * sizeof(float)));
-    void* split_ws = static_cast<uint8_t*>(ws) + pad256((size_t)M * sizeof(float)) + umma_xh_bytes(w, M);
+    unsigned* tickets = static_cast<unsigned*>(ws);
+    uint8_t* head = static_cast<uint8_t*>(ws) + ws_ticket_bytes(w->N);
+    float* xs = reinterpret_cast<float*>(head);
+    __half* xh = reinterpret_cast<__half*>(head + pad256((size_t)M * sizeof(float)));
+    void* part = head + pad256((size_t)M * sizeof(float)) + umma_xh_bytes(w, M);
     if (umma_sk_supported(w, M)) {
       const int bn = umma_sk_bn(M);
       QG_CUDA_RET(launch_xprep(X, M, (M + bn - 1) / bn * bn, (int)w->K, 0, 1, bn, xh, xs, s));
-      return gemm_umma_sk(w, xh, xs, M, Y, f32, split_ws, sm_count_or_zero(), s, tp);
+      return gemm_umma_sk(w, xh, xs, M, Y, f32, tickets, part, sm_count_or_zero(), s, tp);
     }
     if (tp) return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "gemm: no tensor-parallel output on this path");
     QG_CUDA_RET(launch_xprep(X, M, M, (int)w->K, 0, 0, 0, xh, xs, s));
-    return gemm_umma_ts(w, xh, xs, M, Y, f32, umma_split_count(w, M), split_ws, s);
+    return gemm_umma_ts(w, xh, xs, M, Y, f32, umma_split_count(w, M), tickets, part, s);
   }
   if (gemv_tma_supported(w, M < kMaxM ? M : kMaxM)) {
     // TMA-fed decode kernel (gemv_tma.cu): X preparation + GEMM per 16
@@ -942,4 +943,116 @@ extern "C" qgemm_status_t qgemm_gemm_w4a16_noalloc(const qgemm_weights_t* w, con
   if (st != QGEMM_OK) return st;
   QG_CUDA_RET(cudaMemsetAsync(base, 0, L.first.counter_bytes, s));
   return ldg_run(w, X, M, Y, false, base, L, s, "gemm_noalloc");
+}
+
+// ---------------------------------------------------------------------------
+// Grouped GEMM (mixture of experts)
+// ---------------------------------------------------------------------------
+//
+// E experts of one format and shape; expert e multiplies its M[e] rows of X
+// (rows offs[e] ..) and writes the same rows of Y.  Decode-sized experts
+// (MXFP4 / NVFP4, 1 <= M[e] <= 16) run kGroupChunk at a time through the
+// TMA-fed decode kernel with one stream-K iteration space over all their
+// units, so a step with many small experts pays two launches and one pipeline
+// fill per chunk instead of per expert; every other expert runs as a
+// regular call.  All of them share one workspace (tickets at its start).
+
+namespace qg {
+
+size_t gemv_tma_group_workspace(const qgemm_weights_t* w, int sm_count);
+qgemm_status_t gemm_gemv_tma_group(const qgemm_weights_t* const* w, const int* M, const size_t* row0, int n,
+                                   const uint16_t* X, uint16_t* Y, void* ws, int sm_count, cudaStream_t s);
+constexpr int kGroupChunk = 32;  // problems per fused launch (the kernel's parameter block holds 32)
+
+static bool grouped_fused(const qgemm_weights_t* w, int m) {
+  return m >= 1 && m <= kMaxM && gemv_tma_supported(w, m);
+}
+
+// Workspace for calls whose experts have at most max_m rows: the fused
+// launches' and every regular call's, maximised over the experts' pointer
+// alignments (which select kernels) and over 1 .. max_m rows.
+static size_t grouped_workspace(const qgemm_weights_t* w, int E, int max_m) {
+  if (!w || E < 1 || max_m < 1) return 0;
+  const int sms = sm_count_or_zero();
+  if (sms <= 0) return 0;
+  size_t need = ws_ticket_bytes(w[0].N);
+  unsigned seen = 0;  // alignment classes done: data 32-byte aligned x scales address mod 16
+  for (int e = 0; e < E; ++e) {
+    const uintptr_t d = reinterpret_cast<uintptr_t>(w[e].data), sc = reinterpret_cast<uintptr_t>(w[e].scales);
+    const unsigned cls = ((d & 31u) == 0 ? 16u : 0u) | (unsigned)(sc & 15u);
+    if (seen & (1u << cls)) continue;
+    seen |= 1u << cls;
+    for (int m = 1; m <= max_m; ++m) {
+      const size_t b = grouped_fused(&w[e], m) ? gemv_tma_group_workspace(&w[e], sms) : gemm_decode_workspace(&w[e], m);
+      if (b == 0) return 0;
+      if (b > need) need = b;
+    }
+  }
+  return need;
+}
+
+static qgemm_status_t grouped_gemm(const qgemm_weights_t* w, int E, const uint16_t* X, const int32_t* M,
+                                   const int64_t* offs, uint16_t* Y, void* ws, size_t ws_bytes, cudaStream_t s) {
+  if (E < 0) return fail(QGEMM_ERR_INVALID_ARG, "grouped_gemm: E must be >= 0");
+  if (E == 0) return QGEMM_OK;
+  if (!w || !X || !Y || !M || !offs) return fail(QGEMM_ERR_INVALID_ARG, "grouped_gemm: null pointer");
+  int max_m = 0;
+  for (int e = 0; e < E; ++e) {
+    const qgemm_weights_t& we = w[e];
+    if (we.format != w[0].format || we.N != w[0].N || we.K != w[0].K)
+      return fail(QGEMM_ERR_INVALID_ARG, "grouped_gemm: expert %d differs from expert 0 in format or shape", e);
+    if (M[e] < 0 || offs[e] < 0)
+      return fail(QGEMM_ERR_INVALID_ARG, "grouped_gemm: expert %d has M %d, row offset %lld", e, M[e],
+                  (long long)offs[e]);
+    if (M[e] > max_m) max_m = M[e];
+  }
+  if (max_m == 0) return QGEMM_OK;
+  const int sms = sm_count_or_zero();
+  const size_t need = grouped_workspace(w, E, max_m);
+  if (sms <= 0 || need == 0) return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "grouped_gemm: no plan for this shape");
+  if (!ws || !al16(ws) || ws_bytes < need)
+    return fail(QGEMM_ERR_WORKSPACE, "grouped_gemm: 16-byte aligned workspace of %zu bytes needed, %zu given", need,
+                ws_bytes);
+  const size_t N = w[0].N, K = w[0].K;
+  const qgemm_weights_t* cw[kGroupChunk];
+  int cm[kGroupChunk];
+  size_t cr[kGroupChunk];
+  int n = 0;
+  auto flush = [&]() -> qgemm_status_t {
+    if (n == 0) return QGEMM_OK;
+    const qgemm_status_t st = gemm_gemv_tma_group(cw, cm, cr, n, X, Y, ws, sms, s);
+    n = 0;
+    return st;
+  };
+  for (int e = 0; e < E; ++e) {
+    if (M[e] == 0) continue;
+    const qgemm_weights_t* we = &w[e];
+    if (!we->data || !we->scales || we->reserved != 0 ||
+        (we->format == QGEMM_FMT_NVFP4 && !std::isfinite(we->tensor_scale)) || !al16(we->data))
+      return fail(QGEMM_ERR_INVALID_ARG, "grouped_gemm: expert %d: null or misaligned weights, or bad tensor_scale", e);
+    if (grouped_fused(we, M[e]) && al16(X)) {
+      cw[n] = we; cm[n] = M[e]; cr[n] = (size_t)offs[e];
+      if (++n == kGroupChunk) {
+        const qgemm_status_t st = flush();
+        if (st != QGEMM_OK) return st;
+      }
+    } else {
+      const qgemm_status_t st = gemm_decode(we, X + (size_t)offs[e] * K, M[e], Y + (size_t)offs[e] * N, false, ws,
+                                            ws_bytes, s);
+      if (st != QGEMM_OK) return st;
+    }
+  }
+  return flush();
+}
+
+}  // namespace qg
+
+extern "C" size_t qgemm_grouped_workspace_size(const qgemm_weights_t* w, int32_t E, int32_t max_m) {
+  return qg::grouped_workspace(w, E, max_m);
+}
+
+extern "C" qgemm_status_t qgemm_grouped_gemm_w4a16(const qgemm_weights_t* w, int32_t E, const uint16_t* X,
+                                                   const int32_t* M, const int64_t* offs, uint16_t* Y, void* ws,
+                                                   size_t ws_bytes, void* stream) {
+  return qg::grouped_gemm(w, E, X, M, offs, Y, ws, ws_bytes, qg::as_stream(stream));
 }

@@ -42,6 +42,17 @@ __device__ __forceinline__ void mma_f16_z(float (&d)[4], uint32_t a0, uint32_t a
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
 }
 
+// Split-tile ticket: atomicAdd(p, 1) with acquire-release semantics at GPU
+// scope.  Taken by one thread after a barrier of the threads that stored the
+// partial sums (the release is cumulative over what the barrier ordered), it
+// publishes those stores; for the last contributor its acquire orders the
+// partial loads that follow the next barrier.
+__device__ __forceinline__ unsigned ticket_acq_rel(unsigned* p) {
+  unsigned old;
+  asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(p) : "memory");
+  return old;
+}
+
 __device__ __forceinline__ uint4 ldg_stream16(const void* p) {  // read once: skip L1
   uint4 v;
   asm("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"

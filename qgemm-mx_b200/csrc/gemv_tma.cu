@@ -52,6 +52,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstring>
+
 #include "common.cuh"
 #include "gemv_core.cuh"
 #include "tc.cuh"
@@ -86,7 +88,9 @@ struct GtCfg {
   // the W box lands on a 1024-byte boundary (128-byte swizzle); the unit's X
   // image and its row factors are one bulk copy into [X | XF]
   static_assert(W_BYTES % 1024 == 0 && XF_BYTES >= 4 * MPAD, "stage layout");
-  static constexpr int PART_BYTES = (UG - 1) * kGtGroups * NT * 32 * 16;  // other groups' sums
+  // other groups' sums, two buffers by segment parity (group 0 reads one while
+  // the others may already fill the next)
+  static constexpr int PART_BYTES = 2 * (UG - 1) * kGtGroups * NT * 32 * 16;
   static constexpr int STAGES = ((200 * 1024 - PART_BYTES) / STAGE) & ~1;  // even: two producers
   static constexpr int BYTES = 1024 + STAGES * STAGE + 2 * STAGES * 8 + 16 + PART_BYTES;
   static_assert(BYTES <= 232448, "shared memory");
@@ -94,17 +98,30 @@ struct GtCfg {
 };
 
 struct GtArgs {
-  const uint8_t* scales;
-  const uint8_t* xg;     // k_xprep_units image: per 256-k unit, mpad rows x 512 B then mpad row factors
-  void* Y;
   float* partials;       // [2 * G][8 row groups][NT][32 lanes] float4
-  unsigned* counters;    // [tiles]
-  long long T;           // tiles * KS
-  int M, N, K, ldy;
+  unsigned* counters;    // [n_exp * tiles]
+  long long T;           // n_exp * tiles * KS
+  int N, K, ldy;         // every problem of the launch: W [N, K]; Y rows ldy apart
+  int tiles;             // 128-row tiles per problem
   int KS;                // units per tile (K / 256)
   int G;
-  float ts;
   TpOut tp;              // world > 0: store into every rank's Y_full, then tp_finish
+};
+
+// The problems of one launch: one (MAXE = 1) or up to kGtMaxExperts weight
+// matrices of the same format and shape (a mixture-of-experts layer), each
+// with its own activations and output.  Global tile gt = e * tiles + t of the
+// stream-K iteration space belongs to problem e.  Passed as a grid-constant
+// parameter, so the TMA descriptors live in parameter space.
+constexpr int kGtMaxExperts = 32;
+template <int MAXE>
+struct GtGroup {
+  CUtensorMap map_w[MAXE];   // packed codes, box 128 rows x 128 B, 128-byte swizzle
+  const uint8_t* scales[MAXE];
+  const uint8_t* xg[MAXE];   // k_xprep_units image: per 256-k unit, mpad rows x 512 B then mpad row factors
+  void* Y[MAXE];
+  int M[MAXE];               // activation rows (<= mpad)
+  float ts[MAXE];            // NVFP4 tensor scale
 };
 
 // ---------------------------------------------------------------------------
@@ -117,8 +134,18 @@ struct GtArgs {
 // 2^s (rows >= M: zeros and factor 0).
 // ---------------------------------------------------------------------------
 constexpr int kXuWarps = 8;
-__global__ void __launch_bounds__(kXuWarps * 32) k_xprep_units(const uint16_t* __restrict__ X, int M, int K, int mpad,
-                                                              int fmt, uint8_t* __restrict__ img) {
+template <int MAXE>
+struct XuGroup {             // problem e = blockIdx.y: X [M[e]][K] and its image
+  const uint16_t* X[MAXE];
+  uint8_t* img[MAXE];
+  int M[MAXE];
+};
+template <int MAXE>
+__global__ void __launch_bounds__(kXuWarps * 32) k_xprep_units(const __grid_constant__ XuGroup<MAXE> xu, int K, int mpad,
+                                                              int fmt) {
+  const uint16_t* __restrict__ X = xu.X[MAXE == 1 ? 0 : blockIdx.y];
+  uint8_t* __restrict__ img = xu.img[MAXE == 1 ? 0 : blockIdx.y];
+  const int M = xu.M[MAXE == 1 ? 0 : blockIdx.y];
   // Dependents (the GEMM) may launch at once and stream their weights; they
   // read the image only after their own wait, which covers this grid.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -156,9 +183,9 @@ __global__ void __launch_bounds__(kXuWarps * 32) k_xprep_units(const uint16_t* _
   if (lane == 0) reinterpret_cast<float*>(unit + mpad * (kGtUnitK * 2))[m] = f;
 }
 
-template <int FMT, int NT, int RPW, int UG, bool F32OUT>
+template <int FMT, int NT, int RPW, int UG, bool F32OUT, int MAXE>
 __global__ void __launch_bounds__(GtCfg<FMT, NT, RPW, UG>::THREADS, 1)
-k_gemv_tma(const __grid_constant__ CUtensorMap map_w, const GtArgs a) {
+k_gemv_tma(const __grid_constant__ GtGroup<MAXE> pg, const GtArgs a) {
   using C = GtCfg<FMT, NT, RPW, UG>;
   constexpr int kGtCons = C::CONS;
   constexpr int S = C::STAGES;
@@ -175,7 +202,7 @@ k_gemv_tma(const __grid_constant__ CUtensorMap map_w, const GtArgs a) {
   auto full_bar = [&](int s) { return su32(&bars[s]); };
   auto empty_bar = [&](int s) { return su32(&bars[S + s]); };
   unsigned* s_ticket = reinterpret_cast<unsigned*>(bars + 2 * S);
-  float4* s_part = reinterpret_cast<float4*>(bars + 2 * S + 2);  // [UG - 1][8 row groups][NT][32]
+  float4* s_part = reinterpret_cast<float4*>(bars + 2 * S + 2);  // [2][UG - 1][8 row groups][NT][32]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long it0 = (long long)blockIdx.x * a.T / a.G;
@@ -206,12 +233,16 @@ k_gemv_tma(const __grid_constant__ CUtensorMap map_w, const GtArgs a) {
       p_ks += kGtProd;
       while (p_ks >= KS) { p_ks -= KS; ++p_tile; }
     };
+    // problem of global tile gt and its tile within the problem
+    auto prob = [&](int gt) { return MAXE == 1 ? 0 : gt / a.tiles; };
+    auto ltile = [&](int gt) { return MAXE == 1 ? gt : gt - (gt / a.tiles) * a.tiles; };
     auto issue_w = [&](int s) {  // lane 0: the unit's packed-W box; its X follows on the same barrier
       mbar_expect_tx(full_bar(s), (uint32_t)(C::W_BYTES + C::X_BYTES + C::XF_BYTES));
-      tma_load_2d(base + (uint32_t)W_off(s), &map_w, p_ks * (kGtUnitK / 2), p_tile * kGtRows, full_bar(s));
+      tma_load_2d(base + (uint32_t)W_off(s), &pg.map_w[prob(p_tile)], p_ks * (kGtUnitK / 2), ltile(p_tile) * kGtRows,
+                  full_bar(s));
     };
-    auto issue_x = [&](int s, int ks) {  // lane 0: the unit's f16 X image and row factors (k_xprep_units)
-      const uint8_t* src = a.xg + (size_t)ks * (C::X_BYTES + C::XF_BYTES);
+    auto issue_x = [&](int s, int gt, int ks) {  // lane 0: the unit's f16 X image and row factors (k_xprep_units)
+      const uint8_t* src = pg.xg[prob(gt)] + (size_t)ks * (C::X_BYTES + C::XF_BYTES);
       asm volatile(
           "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
           ::"r"(base + (uint32_t)X_off(s)), "l"(src), "r"((uint32_t)(C::X_BYTES + C::XF_BYTES)), "r"(full_bar(s))
@@ -223,16 +254,17 @@ k_gemv_tma(const __grid_constant__ CUtensorMap map_w, const GtArgs a) {
 #pragma unroll
       for (int q = 0; q < kGtRows / 32; ++q) {
         const int row = lane + 32 * q;
-        int n = p_tile * kGtRows + row;
+        int n = ltile(p_tile) * kGtRows + row;
         n = n < a.N ? n : a.N - 1;  // rows past N: TMA zero-fills their codes
-        const uint8_t* src = a.scales + (size_t)n * srow + (size_t)p_ks * C::SB;
+        const uint8_t* src = pg.scales[prob(p_tile)] + (size_t)n * srow + (size_t)p_ks * C::SB;
         const uint32_t dst = base + (uint32_t)(S_off(s) + row * C::SB);
         if (FMT == 0) asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
         else asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
       }
       asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(full_bar(s)) : "memory");
     };
-    if (lane == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_w)) : "memory");
+    if (lane == 0 && MAXE == 1)
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&pg.map_w[0])) : "memory");
     const int pre = niter < S ? niter : S;
     // Weights and scales do not depend on the previous grid: the first stages'
     // go out before the programmatic-launch wait; X follows it.
@@ -243,13 +275,13 @@ k_gemv_tma(const __grid_constant__ CUtensorMap map_w, const GtArgs a) {
     }
     asm volatile("griddepcontrol.wait;" ::: "memory");  // the X image is the preparation grid's output
     if (lane == 0)
-      for (int i = p; i < pre; i += kGtProd) issue_x(i % S, (int)((it0 + i) % KS));
+      for (int i = p; i < pre; i += kGtProd) issue_x(i % S, (int)((it0 + i) / KS), (int)((it0 + i) % KS));
     for (int i = pre + ((p - pre % kGtProd + kGtProd) % kGtProd); i < niter; i += kGtProd) {
       const int s = i % S;
       if (lane == 0) ok = mbar_wait_flag(empty_bar(s), ((i / S) + 1) & 1, fault);
       ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
       if (!ok) break;
-      if (lane == 0) { issue_w(s); issue_x(s, p_ks); }
+      if (lane == 0) { issue_w(s); issue_x(s, p_tile, p_ks); }
       issue_scales(s);
       advance();
     }
@@ -280,20 +312,25 @@ k_gemv_tma(const __grid_constant__ CUtensorMap map_w, const GtArgs a) {
     };
     auto grp = [&](int r) { return RPW * wq + r; };  // 16-row group of row tile r within the tile
     auto store = [&](int tile, float (&v)[RPW][NT][4]) {
+      const int pe = MAXE == 1 ? 0 : tile / a.tiles;        // problem of global tile `tile`
+      const int lt = MAXE == 1 ? tile : tile - pe * a.tiles;
+      void* Yp = pg.Y[pe];
+      const int Mp = pg.M[pe];
+      const float ts = pg.ts[pe];
 #pragma unroll
       for (int r = 0; r < RPW; ++r)
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const int n = tile * kGtRows + 16 * grp(r) + g + ((e & 2) ? 8 : 0);
+            const int n = lt * kGtRows + 16 * grp(r) + g + ((e & 2) ? 8 : 0);
             const int m = 8 * t + 2 * j + (e & 1);
-            if (n < a.N && m < a.M) {
+            if (n < a.N && m < Mp) {
               float y = v[r][t][e];
-              if (FMT == 1) y *= a.ts;
-              if (F32OUT) static_cast<float*>(a.Y)[(size_t)m * a.ldy + n] = y;
+              if (FMT == 1) y *= ts;
+              if (F32OUT) static_cast<float*>(Yp)[(size_t)m * a.ldy + n] = y;
               else if (a.tp.world > 0) tp_store(a.tp, (size_t)m, n, __float2bfloat16_rn(y));
-              else static_cast<__nv_bfloat16*>(a.Y)[(size_t)m * a.ldy + n] = __float2bfloat16_rn(y);
+              else static_cast<__nv_bfloat16*>(Yp)[(size_t)m * a.ldy + n] = __float2bfloat16_rn(y);
             }
           }
         }
@@ -311,15 +348,16 @@ k_gemv_tma(const __grid_constant__ CUtensorMap map_w, const GtArgs a) {
 #pragma unroll
         for (int t = 0; t < NT; ++t)
           __stcg(mine + (grp(r) * NT + t) * 32 + lane, make_float4(acc[r][t][0], acc[r][t][1], acc[r][t][2], acc[r][t][3]));
-      __threadfence();
+      // one acquire-release ticket after the group's barrier orders every
+      // thread's partial stores before it and the last contributor's loads
+      // after it (the release is cumulative over what the barrier ordered)
       asm volatile("bar.sync 1, %0;" ::"r"(WPG * 32) : "memory");
-      if (wq == 0 && lane == 0) *s_ticket = atomicAdd(a.counters + tile, 1u);  // also after a timeout: the tickets still return to zero
+      if (wq == 0 && lane == 0) *s_ticket = ticket_acq_rel(a.counters + tile);  // also after a timeout: the tickets still return to zero
       asm volatile("bar.sync 1, %0;" ::"r"(WPG * 32) : "memory");
       const unsigned ticket = *s_ticket;
       const long long t0 = (long long)tile * KS, t1 = t0 + KS - 1;
       const int c_lo = (int)(((t0 + 1) * a.G - 1) / a.T), c_hi = (int)(((t1 + 1) * a.G - 1) / a.T);
       if (ticket == (unsigned)(c_hi - c_lo)) {  // last contributor: sum in CTA order
-        __threadfence();
         float sum[RPW][NT][4];
         zero(sum);
         // CB contributors' partials in flight before the first add (they come
@@ -356,6 +394,7 @@ k_gemv_tma(const __grid_constant__ CUtensorMap map_w, const GtArgs a) {
       asm volatile("bar.sync 1, %0;" ::"r"(WPG * 32) : "memory");  // s_ticket is reused
     };
 
+    int segp = 0;        // s_part buffer of the current segment
     long long it = it0;  // global index of the segment's first unit
     int ib = 0;          // its index in this CTA's range
     while (ib < niter) {
@@ -427,7 +466,7 @@ k_gemv_tma(const __grid_constant__ CUtensorMap map_w, const GtArgs a) {
           for (int r = 0; r < RPW; ++r)
 #pragma unroll
             for (int t = 0; t < NT; ++t)
-              s_part[(((ug - 1) * kGtGroups + grp(r)) * NT + t) * 32 + lane] =
+              s_part[((((segp * (UG - 1)) + ug - 1) * kGtGroups + grp(r)) * NT + t) * 32 + lane] =
                   make_float4(acc[r][t][0], acc[r][t][1], acc[r][t][2], acc[r][t][3]);
         }
         asm volatile("bar.sync 2, %0;" ::"r"(kGtCons * 32) : "memory");
@@ -437,13 +476,15 @@ k_gemv_tma(const __grid_constant__ CUtensorMap map_w, const GtArgs a) {
             for (int r = 0; r < RPW; ++r)
 #pragma unroll
               for (int t = 0; t < NT; ++t) {
-                const float4 h = s_part[(((gg - 1) * kGtGroups + grp(r)) * NT + t) * 32 + lane];
+                const float4 h = s_part[((((segp * (UG - 1)) + gg - 1) * kGtGroups + grp(r)) * NT + t) * 32 + lane];
                 acc[r][t][0] += h.x; acc[r][t][1] += h.y; acc[r][t][2] += h.z; acc[r][t][3] += h.w;
               }
         }
       }
       if (ug == 0) flush(tile, ks0 == 0 && len == KS);
-      if (UG > 1) asm volatile("bar.sync 2, %0;" ::"r"(kGtCons * 32) : "memory");  // s_part is reused
+      // (no barrier here: the next segment's sums go to the other s_part buffer,
+      // and group 0 passes the next segment's barrier only after reading this one)
+      segp ^= 1;
       zero(acc);
       it += len;
       ib += len;
@@ -481,22 +522,23 @@ bool gemv_tma_supported(const qgemm_weights_t* w, int mb) {
 struct GtPlan {
   int nt, mpad, tiles, KS, G;
   long long T;
-  size_t counter_bytes, partial_bytes, image_bytes;
+  size_t counter_bytes, partial_bytes, image_bytes;  // image_bytes: one problem's
 };
-static GtPlan gt_plan(const qgemm_weights_t* w, int mb, int sm_count) {
+// Plan for n_exp problems of w's shape with at most mb activation rows each.
+static GtPlan gt_plan(const qgemm_weights_t* w, int mb, int sm_count, int n_exp = 1) {
   GtPlan p;
   p.nt = mb <= 8 ? 1 : 2;
   p.mpad = 8 * p.nt;
   p.tiles = (int)((w->N + kGtRows - 1) / kGtRows);
   p.KS = (int)(w->K / kGtUnitK);
-  p.T = (long long)p.tiles * p.KS;
+  p.T = (long long)n_exp * p.tiles * p.KS;
   p.G = (int)(p.T < sm_count ? p.T : sm_count);
-  p.counter_bytes = ((size_t)p.tiles * sizeof(unsigned) + 255) & ~(size_t)255;
+  p.counter_bytes = ws_ticket_bytes(w->N);  // holds n_exp * tiles <= 32 * tiles tickets
   p.partial_bytes = (((size_t)2 * p.G * kGtGroups * p.nt * 32 * sizeof(float4)) + 255) & ~(size_t)255;
   p.image_bytes = (((size_t)p.KS * (p.mpad * kGtUnitK * 2 + 128)) + 255) & ~(size_t)255;
   return p;
 }
-// [counters | partials | X image], sized for 16 activation rows (two n-tiles)
+// [tickets | partials | X image], sized for 16 activation rows (two n-tiles)
 size_t gemv_tma_workspace(const qgemm_weights_t* w, int sm_count) {
   const GtPlan p = gt_plan(w, 16, sm_count);
   return p.counter_bytes + p.partial_bytes + p.image_bytes;
@@ -512,8 +554,8 @@ constexpr int gt_rpw() { return NT == 1 ? 2 : 1; }
 template <int NT>
 constexpr int gt_ug() { return NT == 1 ? 3 : 1; }
 
-template <int FMT, int NT, bool F32>
-static cudaError_t launch_gt_t(const CUtensorMap& mw, const GtArgs& a, cudaStream_t s) {
+template <int FMT, int NT, bool F32, int MAXE>
+static cudaError_t launch_gt_t(const GtGroup<MAXE>& g, const GtArgs& a, cudaStream_t s) {
   constexpr int BYTES = GtCfg<FMT, NT, gt_rpw<NT>(), gt_ug<NT>()>::BYTES;
   static bool attr[64] = {false};
   int dev = 0;
@@ -521,7 +563,8 @@ static cudaError_t launch_gt_t(const CUtensorMap& mw, const GtArgs& a, cudaStrea
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr[dev]) {
-    e = cudaFuncSetAttribute(k_gemv_tma<FMT, NT, gt_rpw<NT>(), gt_ug<NT>(), F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, BYTES);
+    e = cudaFuncSetAttribute(k_gemv_tma<FMT, NT, gt_rpw<NT>(), gt_ug<NT>(), F32, MAXE>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, BYTES);
     if (e != cudaSuccess) return e;
     attr[dev] = true;
   }
@@ -535,7 +578,37 @@ static cudaError_t launch_gt_t(const CUtensorMap& mw, const GtArgs& a, cudaStrea
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k_gemv_tma<FMT, NT, gt_rpw<NT>(), gt_ug<NT>(), F32>, mw, a);
+  return cudaLaunchKernelEx(&cfg, k_gemv_tma<FMT, NT, gt_rpw<NT>(), gt_ug<NT>(), F32, MAXE>, g, a);
+}
+
+template <int MAXE>
+static cudaError_t launch_gt(int fmt, int nt, bool f32, const GtGroup<MAXE>& g, const GtArgs& a, cudaStream_t s) {
+  if (fmt == QGEMM_FMT_MXFP4) {
+    if (nt == 1) return f32 ? launch_gt_t<0, 1, true, MAXE>(g, a, s) : launch_gt_t<0, 1, false, MAXE>(g, a, s);
+    return f32 ? launch_gt_t<0, 2, true, MAXE>(g, a, s) : launch_gt_t<0, 2, false, MAXE>(g, a, s);
+  }
+  if (nt == 1) return f32 ? launch_gt_t<1, 1, true, MAXE>(g, a, s) : launch_gt_t<1, 1, false, MAXE>(g, a, s);
+  return f32 ? launch_gt_t<1, 2, true, MAXE>(g, a, s) : launch_gt_t<1, 2, false, MAXE>(g, a, s);
+}
+
+template <int MAXE>
+static cudaError_t launch_xprep_units(const XuGroup<MAXE>& xu, int n_exp, const GtPlan& p, int K, int fmt,
+                                      cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((p.mpad * p.KS + kXuWarps - 1) / kXuWarps), (unsigned)n_exp);
+  cfg.blockDim = dim3(kXuWarps * 32);
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_xprep_units<MAXE>, xu, K, p.mpad, fmt == QGEMM_FMT_MXFP4 ? 0 : 1);
+}
+
+static bool gt_map(CUtensorMap* m, const qgemm_weights_t* w) {
+  return make_tma_map_2d(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->data, w->K / 2, w->N, w->K / 2, kGtUnitK / 2, kGtRows,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 // Two launches over mb <= 16 activation rows X (bf16 [mb][K], 16-byte
@@ -545,48 +618,81 @@ qgemm_status_t gemm_gemv_tma(const qgemm_weights_t* w, const uint16_t* X, int mb
                              void* ws, int sm_count, cudaStream_t s, const TpOut* tp) {
   if (!gemv_tma_supported(w, mb)) return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "TMA decode path: unsupported shape");
   if (sm_count <= 0) return fail(QGEMM_ERR_CUDA, "TMA decode path: no device properties");
+  if (tp && f32) return fail(QGEMM_ERR_INVALID_ARG, "TMA decode path: tensor-parallel output is bf16");
   const GtPlan p = gt_plan(w, mb, sm_count);
-  CUtensorMap mw;
-  if (!make_tma_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->data, w->K / 2, w->N, w->K / 2, kGtUnitK / 2, kGtRows,
-                       CU_TENSOR_MAP_SWIZZLE_128B))
-    return fail(QGEMM_ERR_CUDA, "TMA decode path: cuTensorMapEncodeTiled failed");
+  GtGroup<1> g;
+  if (!gt_map(&g.map_w[0], w)) return fail(QGEMM_ERR_CUDA, "TMA decode path: cuTensorMapEncodeTiled failed");
   uint8_t* img = static_cast<uint8_t*>(ws) + p.counter_bytes + p.partial_bytes;
-  {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)((p.mpad * p.KS + kXuWarps - 1) / kXuWarps));
-    cfg.blockDim = dim3(kXuWarps * 32);
-    cfg.stream = s;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, k_xprep_units, X, mb, (int)w->K, p.mpad,
-                                             w->format == QGEMM_FMT_MXFP4 ? 0 : 1, img);
-    if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "TMA decode X preparation: %s", cudaGetErrorString(e));
-  }
+  XuGroup<1> xu;
+  xu.X[0] = X; xu.img[0] = img; xu.M[0] = mb;
+  cudaError_t e = launch_xprep_units<1>(xu, 1, p, (int)w->K, w->format, s);
+  if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "TMA decode X preparation: %s", cudaGetErrorString(e));
+  g.scales[0] = static_cast<const uint8_t*>(w->scales);
+  g.xg[0] = img;
+  g.Y[0] = Y;
+  g.M[0] = mb;
+  g.ts[0] = w->tensor_scale;
   GtArgs a;
-  a.scales = static_cast<const uint8_t*>(w->scales);
-  a.xg = img;
-  a.Y = Y;
   a.counters = static_cast<unsigned*>(ws);
   a.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + p.counter_bytes);
-  a.T = p.T; a.M = mb; a.N = (int)w->N; a.K = (int)w->K; a.ldy = ldy;
-  a.KS = p.KS; a.G = p.G; a.ts = w->tensor_scale;
+  a.T = p.T; a.N = (int)w->N; a.K = (int)w->K; a.ldy = ldy; a.tiles = p.tiles;
+  a.KS = p.KS; a.G = p.G;
   a.tp = {};
-  if (tp) {
-    if (f32) return fail(QGEMM_ERR_INVALID_ARG, "TMA decode path: tensor-parallel output is bf16");
-    a.tp = *tp;
-  }
-  cudaError_t e;
-  if (w->format == QGEMM_FMT_MXFP4) {
-    if (p.nt == 1) e = f32 ? launch_gt_t<0, 1, true>(mw, a, s) : launch_gt_t<0, 1, false>(mw, a, s);
-    else e = f32 ? launch_gt_t<0, 2, true>(mw, a, s) : launch_gt_t<0, 2, false>(mw, a, s);
-  } else {
-    if (p.nt == 1) e = f32 ? launch_gt_t<1, 1, true>(mw, a, s) : launch_gt_t<1, 1, false>(mw, a, s);
-    else e = f32 ? launch_gt_t<1, 2, true>(mw, a, s) : launch_gt_t<1, 2, false>(mw, a, s);
-  }
+  if (tp) a.tp = *tp;
+  e = launch_gt<1>(w->format, p.nt, f32, g, a, s);
   if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "TMA decode launch: %s", cudaGetErrorString(e));
+  return QGEMM_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Grouped decode (mixture of experts): problems e = 0 .. n - 1 of the same
+// format and shape, problem e's activations X + row0[e] K ([M[e]][K]) and
+// output Y + row0[e] N.  Up to kGtMaxExperts problems per pair of launches;
+// all problems' units share one stream-K iteration space, so small experts
+// do not each pay a launch and a pipeline fill.
+// ---------------------------------------------------------------------------
+
+// Workspace of one launch over up to kGtMaxExperts problems with mpad = 16.
+size_t gemv_tma_group_workspace(const qgemm_weights_t* w, int sm_count) {
+  const GtPlan p = gt_plan(w, 16, sm_count, kGtMaxExperts);
+  return p.counter_bytes + p.partial_bytes + (size_t)kGtMaxExperts * p.image_bytes;
+}
+
+// ws: gemv_tma_group_workspace bytes, counters zero.  Every problem needs
+// 1 <= M[e] <= 16 and gemv_tma_supported.
+qgemm_status_t gemm_gemv_tma_group(const qgemm_weights_t* const* w, const int* M, const size_t* row0, int n,
+                                   const uint16_t* X, uint16_t* Y, void* ws, int sm_count, cudaStream_t s) {
+  if (n < 1 || n > kGtMaxExperts) return fail(QGEMM_ERR_INVALID_ARG, "grouped decode: 1..%d problems", kGtMaxExperts);
+  if (sm_count <= 0) return fail(QGEMM_ERR_CUDA, "grouped decode: no device properties");
+  int mmax = 0;
+  for (int e = 0; e < n; ++e) mmax = M[e] > mmax ? M[e] : mmax;
+  const GtPlan p = gt_plan(w[0], mmax, sm_count, n);
+  uint8_t* img = static_cast<uint8_t*>(ws) + p.counter_bytes + p.partial_bytes;
+  GtGroup<kGtMaxExperts> g;
+  XuGroup<kGtMaxExperts> xu;
+  std::memset(&g, 0, sizeof(g));
+  std::memset(&xu, 0, sizeof(xu));
+  for (int e = 0; e < n; ++e) {
+    if (!gt_map(&g.map_w[e], w[e])) return fail(QGEMM_ERR_CUDA, "grouped decode: cuTensorMapEncodeTiled failed");
+    g.scales[e] = static_cast<const uint8_t*>(w[e]->scales);
+    g.xg[e] = img + (size_t)e * p.image_bytes;
+    g.Y[e] = Y + row0[e] * w[0]->N;
+    g.M[e] = M[e];
+    g.ts[e] = w[e]->tensor_scale;
+    xu.X[e] = X + row0[e] * w[0]->K;
+    xu.img[e] = img + (size_t)e * p.image_bytes;
+    xu.M[e] = M[e];
+  }
+  cudaError_t e = launch_xprep_units<kGtMaxExperts>(xu, n, p, (int)w[0]->K, w[0]->format, s);
+  if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "grouped decode X preparation: %s", cudaGetErrorString(e));
+  GtArgs a;
+  a.counters = static_cast<unsigned*>(ws);
+  a.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + p.counter_bytes);
+  a.T = p.T; a.N = (int)w[0]->N; a.K = (int)w[0]->K; a.ldy = (int)w[0]->N; a.tiles = p.tiles;
+  a.KS = p.KS; a.G = p.G;
+  a.tp = {};
+  e = launch_gt<kGtMaxExperts>(w[0]->format, p.nt, false, g, a, s);
+  if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "grouped decode launch: %s", cudaGetErrorString(e));
   return QGEMM_OK;
 }
 

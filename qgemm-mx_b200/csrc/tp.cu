@@ -92,7 +92,7 @@ size_t qgemm_tp_sync_bytes(int32_t world) {
 size_t qgemm_tp_workspace_size(const qgemm_weights_t* w_local, int32_t M) {
   if (!w_local || M < 1) return 0;
   const size_t inner = gemm_decode_workspace(w_local, M);
-  return pad256_tp((size_t)M * w_local->N * sizeof(uint16_t)) + inner;
+  return pad256_tp(inner) + (size_t)M * w_local->N * sizeof(uint16_t);
 }
 
 qgemm_status_t qgemm_tp_gemm_w4a16(const qgemm_weights_t* w_local, const uint16_t* X, int32_t M, int32_t world,
@@ -121,9 +121,10 @@ qgemm_status_t qgemm_tp_gemm_w4a16(const qgemm_weights_t* w_local, const uint16_
   if (!ws || (reinterpret_cast<uintptr_t>(ws) & 15u) || ws_bytes < need)
     return fail(QGEMM_ERR_WORKSPACE, "tp_gemm: 16-byte aligned workspace of %zu bytes needed, %zu given", need,
                 ws_bytes);
-  uint16_t* slice = static_cast<uint16_t*>(ws);
-  uint8_t* inner = static_cast<uint8_t*>(ws) + pad256_tp((size_t)M * n_loc * sizeof(uint16_t));
-  const size_t inner_bytes = ws_bytes - (size_t)(inner - static_cast<uint8_t*>(ws));
+  // [GEMM workspace (tickets first) | this rank's Y slice]
+  uint8_t* inner = static_cast<uint8_t*>(ws);
+  const size_t inner_bytes = gemm_decode_workspace(w_local, M);
+  uint16_t* slice = reinterpret_cast<uint16_t*>(inner + pad256_tp(inner_bytes));
   cudaStream_t s = as_stream(stream);
   if (fused_tp(w_local, M))  // the GEMM kernel writes every rank's Y_full and synchronises
     return gemm_decode_ex(w_local, X, M, nullptr, false, inner, inner_bytes, s, &t);

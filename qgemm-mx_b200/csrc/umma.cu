@@ -416,17 +416,20 @@ int umma_splits(const qgemm_weights_t* w, int M, int sm_count) {
   long long s = slots / (tiles > 0 ? tiles : 1);
   const long long kmax = (long long)(w->K / kUBK) / 8;
   if (s > kmax) s = kmax;
+  // split tiles take one ticket each in the workspace's ticket region (fewer
+  // than sm_count tiles whenever s >= 2)
+  if ((size_t)tiles * sizeof(unsigned) > ws_ticket_bytes(w->N)) s = 1;
   return s < 1 ? 1 : (int)s;
 }
 size_t umma_split_workspace(const qgemm_weights_t* w, int M, int splits) {
   if (splits <= 1) return 0;
   const int bn = umma_bn_for(M);
   const size_t tiles = ((w->N + kUBM - 1) / kUBM) * (size_t)((M + bn - 1) / bn);
-  return ((tiles * sizeof(unsigned) + 255) & ~(size_t)255) + tiles * (size_t)splits * bn * kUBM * sizeof(float);
+  return tiles * (size_t)splits * bn * kUBM * sizeof(float);
 }
 
 qgemm_status_t gemm_umma_ts(const qgemm_weights_t* w, const __half* Xh, const float* xs, int M, void* Y, bool f32,
-                            int splits, void* split_ws, cudaStream_t s) {
+                            int splits, unsigned* tickets, void* partials, cudaStream_t s) {
   if (w->format != QGEMM_FMT_MXFP4 && w->format != QGEMM_FMT_NVFP4)
     return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "umma path: MXFP4 / NVFP4 only");
   if (w->K % kUBK != 0 || w->K > (size_t)INT32_MAX || w->N > (size_t)INT32_MAX)
@@ -444,9 +447,10 @@ qgemm_status_t gemm_umma_ts(const qgemm_weights_t* w, const __half* Xh, const fl
   a.counters = nullptr; a.partials = nullptr;
   if (a.splits > 1) {
     const size_t tiles = ((w->N + kUBM - 1) / kUBM) * (size_t)((M + bn - 1) / bn);
-    a.counters = static_cast<unsigned*>(split_ws);
-    a.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(split_ws) +
-                                          ((tiles * sizeof(unsigned) + 255) & ~(size_t)255));
+    if (tiles * sizeof(unsigned) > ws_ticket_bytes(w->N))
+      return fail(QGEMM_ERR_WORKSPACE, "umma path: %zu split tiles exceed the ticket region", tiles);
+    a.counters = tickets;
+    a.partials = static_cast<float*>(partials);
   }
   cudaError_t e;
   if (w->format == QGEMM_FMT_MXFP4)

@@ -582,11 +582,11 @@ static BsPlan bs_plan(const qgemm_weights_t* w, int M, int sm_count) {
   p.G = (int)(p.T < sm_count ? p.T : sm_count);
   const size_t xstage = (size_t)2 * p.bn * kBsK + 1024;
   p.x_bytes = (((size_t)((M + p.bn - 1) / p.bn) * p.KS * xstage) + 255) & ~(size_t)255;
-  p.counter_bytes = (((size_t)p.tiles * sizeof(unsigned)) + 255) & ~(size_t)255;
+  p.counter_bytes = ws_ticket_bytes(w->N);
   p.partial_bytes = (((size_t)2 * p.G * kBsRows * p.bn * sizeof(float)) + 255) & ~(size_t)255;
   return p;
 }
-// [X image | counters | partials]
+// [tickets | X image | partials]
 size_t umma_bs_workspace(const qgemm_weights_t* w, int M, int sm_count) {
   const BsPlan p = bs_plan(w, M, sm_count);
   return p.x_bytes + p.counter_bytes + p.partial_bytes;
@@ -645,7 +645,9 @@ qgemm_status_t gemm_umma_bs(const qgemm_weights_t* w, const uint16_t* X, int M, 
           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return fail(QGEMM_ERR_CUDA, "block-scaled path: cuTensorMapEncodeTiled failed");
-  uint8_t* img = static_cast<uint8_t*>(ws);
+  if ((size_t)p.tiles * sizeof(unsigned) > p.counter_bytes)
+    return fail(QGEMM_ERR_WORKSPACE, "block-scaled path: %d tiles exceed the ticket region", p.tiles);
+  uint8_t* img = static_cast<uint8_t*>(ws) + p.counter_bytes;
   const int nrows = (M + p.bn - 1) / p.bn * p.bn;
   {
     cudaLaunchConfig_t cfg = {};
@@ -665,8 +667,8 @@ qgemm_status_t gemm_umma_bs(const qgemm_weights_t* w, const uint16_t* X, int M, 
   a.scales = static_cast<const uint8_t*>(w->scales);
   a.xbs = img;
   a.Y = Y;
-  a.counters = reinterpret_cast<unsigned*>(img + p.x_bytes);
-  a.partials = reinterpret_cast<float*>(img + p.x_bytes + p.counter_bytes);
+  a.counters = static_cast<unsigned*>(ws);
+  a.partials = reinterpret_cast<float*>(img + p.x_bytes);
   a.T = p.T; a.M = M; a.N = (int)w->N; a.K = (int)w->K;
   a.tiles_n = p.tiles_n; a.KS = p.KS; a.G = p.G;
   a.tp = {};

@@ -590,14 +590,15 @@ static SkPlan sk_plan(const qgemm_weights_t* w, int M, int sm_count) {
   p.KS = (int)(w->K / kSkBK);
   p.T = (long long)p.tiles * p.KS;
   p.G = (int)(p.T < sm_count ? p.T : sm_count);
-  p.counter_bytes = ((size_t)p.tiles * sizeof(unsigned) + 255) & ~(size_t)255;
+  p.counter_bytes = (size_t)p.tiles * sizeof(unsigned);  // in the workspace's ticket region
   p.partial_bytes = (size_t)2 * p.G * kSkRows * p.bn * sizeof(float);
   return p;
 }
 
+// The partial-sum block; the tickets live in the workspace's ticket region.
 size_t umma_sk_workspace(const qgemm_weights_t* w, int M, int sm_count) {
   const SkPlan p = sk_plan(w, M, sm_count);
-  return p.counter_bytes + p.partial_bytes;
+  return p.partial_bytes;
 }
 
 template <int FMT, int BN, bool F32>
@@ -632,10 +633,10 @@ static cudaError_t launch_sk_bn(int bn, const CUtensorMap& mw, const SkArgs& a, 
 }
 
 // Xh / xs: the f16 copy of X in the swizzled operand layout and its row
-// factors (k_xprep with swz_bn = umma_sk_bn(M)); ws: the
-// counters + partials block of umma_sk_workspace bytes (counters zero).
+// factors (k_xprep with swz_bn = umma_sk_bn(M)); tickets: the workspace's
+// ticket region (zero); partials: umma_sk_workspace bytes.
 qgemm_status_t gemm_umma_sk(const qgemm_weights_t* w, const __half* Xh, const float* xs, int M, void* Y, bool f32,
-                            void* ws, int sm_count, cudaStream_t s, const TpOut* tp) {
+                            unsigned* tickets, void* partials, int sm_count, cudaStream_t s, const TpOut* tp) {
   if (!umma_sk_supported(w, M)) return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "stream-K tcgen05 path: unsupported shape");
   if (sm_count <= 0) return fail(QGEMM_ERR_CUDA, "stream-K tcgen05 path: no device properties");
   const SkPlan p = sk_plan(w, M, sm_count);
@@ -647,8 +648,10 @@ qgemm_status_t gemm_umma_sk(const qgemm_weights_t* w, const __half* Xh, const fl
   a.scales = static_cast<const uint8_t*>(w->scales);
   a.xsw = reinterpret_cast<const uint8_t*>(Xh);
   a.Y = Y; a.xs = xs;
-  a.counters = static_cast<unsigned*>(ws);
-  a.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + p.counter_bytes);
+  if (p.counter_bytes > ws_ticket_bytes(w->N))
+    return fail(QGEMM_ERR_WORKSPACE, "stream-K tcgen05 path: %d tiles exceed the ticket region", p.tiles);
+  a.counters = tickets;
+  a.partials = static_cast<float*>(partials);
   a.T = p.T; a.M = M; a.N = (int)w->N; a.K = (int)w->K;
   a.tiles_n = p.tiles_n; a.KS = p.KS; a.G = p.G; a.ts = w->tensor_scale;
   a.tp = {};

@@ -78,6 +78,30 @@ def test_argument_checks_return_invalid_arg(qg):
     assert lib.qgemm_gemm_w4a16(C.byref(w), null, 1, null, null, 0, null) == qg.ERR_INVALID_ARG
     assert lib.qgemm_codec_encode(9, null, null, 4, null) == qg.ERR_INVALID_ARG
     assert lib.qgemm_probe_launch(0, null, null, 17, null) == qg.ERR_INVALID_ARG
+
+
+def test_grouped_argument_checks(qg):
+    """qgemm_grouped_gemm_w4a16 rejects mixed shapes and negative counts, and
+    returns at once for E = 0 or all-empty routing, before any device work."""
+    lib = qg.lib()
+    null = C.c_void_p(0)
+    fake = C.c_void_p(1 << 20)  # never dereferenced: every call below returns on the host
+    W3 = qg._Weights * 3
+    ws = W3(qg._Weights(qg.MXFP4, 0, 256, 512, 1 << 20, 1 << 21, 1.0),
+            qg._Weights(qg.MXFP4, 0, 256, 512, 1 << 22, 1 << 23, 1.0),
+            qg._Weights(qg.MXFP4, 0, 128, 512, 1 << 24, 1 << 25, 1.0))
+    I3, O3 = C.c_int32 * 3, C.c_int64 * 3
+    args = lambda E, m, o: (ws, E, fake, I3(*m), O3(*o), fake, null, 0, null)
+    assert lib.qgemm_grouped_gemm_w4a16(*args(0, [1, 1, 1], [0, 1, 2])) == qg.OK
+    assert lib.qgemm_grouped_gemm_w4a16(*args(2, [0, 0, 0], [0, 0, 0])) == qg.OK
+    assert lib.qgemm_grouped_gemm_w4a16(*args(3, [1, 1, 1], [0, 1, 2])) == qg.ERR_INVALID_ARG
+    assert b"expert 2" in lib.qgemm_last_error_message()
+    assert lib.qgemm_grouped_gemm_w4a16(*args(2, [1, -1, 0], [0, 1, 2])) == qg.ERR_INVALID_ARG
+    assert lib.qgemm_grouped_gemm_w4a16(*args(2, [1, 1, 0], [0, -4, 2])) == qg.ERR_INVALID_ARG
+    assert lib.qgemm_grouped_gemm_w4a16(*args(-1, [1, 1, 1], [0, 1, 2])) == qg.ERR_INVALID_ARG
+    assert lib.qgemm_grouped_gemm_w4a16(ws, 2, null, I3(1, 1, 1), O3(0, 1, 2), fake, null, 0, null) \
+        == qg.ERR_INVALID_ARG
+    assert lib.qgemm_grouped_workspace_size(ws, 0, 4) == 0
     assert qg.version().startswith("qgemm-b200")
 
 
