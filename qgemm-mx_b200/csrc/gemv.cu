@@ -635,6 +635,7 @@ int umma_splits(const qgemm_weights_t* w, int M, int sm_count);
 size_t umma_split_workspace(const qgemm_weights_t* w, int M, int splits);  // partials only
 
 bool umma_bs_supported(const qgemm_weights_t* w, int M);
+int umma_bs_launches(const qgemm_weights_t* w, int M, int sm_count);
 size_t umma_bs_workspace(const qgemm_weights_t* w, int M, int sm_count);
 qgemm_status_t gemm_umma_bs(const qgemm_weights_t* w, const uint16_t* X, int M, void* Y, bool f32, void* ws,
                             int sm_count, cudaStream_t s, const TpOut* tp);
@@ -821,7 +822,7 @@ int32_t gemm_launch_count(const qgemm_weights_t* w, int M, int32_t* kernel) {
   int k = 0, n = 0;
   if (umma_bs_supported(w, M)) {
     k = 4;
-    n = 2;  // k_xprep_bs + k_umma_bs
+    n = umma_bs_launches(w, M, sm_count_or_zero());  // k_xprep_bs + k_umma_bs (+ k_bs_fixup for split tiles)
   } else if (use_umma(w, M)) {
     k = umma_sk_supported(w, M) ? 2 : 3;
     n = 2;  // k_xprep + the tcgen05 kernel

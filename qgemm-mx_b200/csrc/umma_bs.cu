@@ -30,8 +30,12 @@
 // MMA is bound by shared-memory reads of A, 4 KB per K = 32.)
 //
 // Schedule: one CTA per SM, stream-K over (tile, sub-step) as in umma_sk.cu:
-// whole tiles are stored directly, split tiles leave FP32 partials and the
-// CTA whose ticket shows it arrived last sums all contributors in CTA order.
+// whole tiles are stored directly; split tiles leave FP32 partials, which
+// k_bs_fixup, launched next, sums in CTA order.  (Summed inside the GEMM by
+// the last contributor of each tile, the partials of a tile went through one
+// CTA's four epilogue warps after its main loop: 10 us with 2 contributors
+// and 47 us with 19 at BN = 64, measured, against 7 us for the whole main
+// loop of a 1024 x 28672 shard.)
 //
 // Warp roles (320 threads), one ring of S stages [W tile | X image | W atom]:
 //   warps 0..3   producers, sub-steps round-robin: lane 0 arms the stage and
@@ -44,8 +48,8 @@
 //                their commits blocked it longer than the MMAs themselves.)
 //   warp 5       TMEM allocation and MMA issue (warp-wide loop, elected lane):
 //                4 MMAs per sub-step, one commit frees the stage.
-//   warps 6..9   epilogue: accumulators (double-buffered) to Y, partials and
-//                split-tile reductions.
+//   warps 6..9   epilogue: accumulators (double-buffered) to Y or to the
+//                split-tile partials.
 // Every mbarrier wait is bounded (tc.cuh); on timeout the kernel sets
 // g_bs_fault, lets copies and MMAs in flight land, frees TMEM and returns.
 #include <cuda.h>
@@ -98,8 +102,8 @@ struct BsArgs {
   const uint8_t* scales;
   const uint8_t* xbs;   // X image of k_xprep_bs: [M blocks][K / 128][X_STAGE]
   void* Y;
-  float* partials;      // [2 * G][128][BN] FP32
-  unsigned* counters;   // [tiles] tickets (start and end at zero)
+  float* partials;      // [2 * G slots][BN / 4 column quads][128 rows] float4
+  int fixup;            // 1: split tiles exist; k_bs_fixup stores them (and runs tp_finish)
   long long T;          // tiles * KS
   int M, N, K;
   int tiles_n;          // tile t -> rows (t % tiles_n) * 128, activations (t / tiles_n) * BN
@@ -231,7 +235,6 @@ k_umma_bs(const __grid_constant__ CUtensorMap map_w, const BsArgs a) {
   auto accf_bar = [&](int b) { return su32(&bars[3 * S + b]); };
   auto acce_bar = [&](int b) { return su32(&bars[3 * S + 2 + b]); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBAR);
-  unsigned* s_ticket = tmem_slot + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long it0 = (long long)blockIdx.x * a.T / a.G;
@@ -411,7 +414,9 @@ k_umma_bs(const __grid_constant__ CUtensorMap map_w, const BsArgs a) {
       const bool whole = (kb == 0 && ke == KS);
       const uint32_t tacc = tmem + t_lane + (uint32_t)(b * C::NB);
       const int slot = 2 * (int)blockIdx.x + (tile == first_tile ? 0 : 1);
-      float* part = a.partials + (size_t)slot * (kBsRows * BN) + (size_t)r * BN;
+      // a split segment's sums: quad q of row r at float4 (q 128 + r), so a
+      // warp's stores (and k_bs_fixup's loads) are contiguous
+      float4* part = reinterpret_cast<float4*>(a.partials) + (size_t)slot * (kBsRows * BN / 4) + r;
       if (ok) {
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 8) {
@@ -441,79 +446,14 @@ k_umma_bs(const __grid_constant__ CUtensorMap map_w, const BsArgs a) {
               }
             }
           } else {
-#pragma unroll
-            for (int u = 0; u < 8; u += 4)
-              __stcg(reinterpret_cast<float4*>(part + c0 + u),
-                     make_float4(u2f(v[u]), u2f(v[u + 1]), u2f(v[u + 2]), u2f(v[u + 3])));
+            __stcg(part + (size_t)(c0 / 4) * kBsRows, make_float4(u2f(v[0]), u2f(v[1]), u2f(v[2]), u2f(v[3])));
+            __stcg(part + (size_t)(c0 / 4 + 1) * kBsRows, make_float4(u2f(v[4]), u2f(v[5]), u2f(v[6]), u2f(v[7])));
           }
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acce_bar(b));  // accumulator buffer free for segment seg + ACC_BUFS
-      if (!whole) {
-        // every epilogue warp takes the same named-barrier steps, also after a timeout
-        __threadfence();
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (warp == kBsEpiWarp0 && lane == 0) *s_ticket = atomicAdd(a.counters + tile, 1u);  // also after a timeout: the tickets still return to zero
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        const unsigned ticket = *s_ticket;
-        const long long t0 = (long long)tile * KS, t1 = t0 + KS - 1;
-        const int c_lo = (int)(((t0 + 1) * a.G - 1) / a.T), c_hi = (int)(((t1 + 1) * a.G - 1) / a.T);
-        if (ticket == (unsigned)(c_hi - c_lo)) {  // last contributor: sum in CTA order
-          __threadfence();
-          // The partials come from L2: up to four contributors' loads of a
-          // 16-column chunk are in flight before the first add (one load and
-          // add per contributor at a time made the tail a chain of L2 round
-          // trips).  The adds stay in CTA order.
-          constexpr int CW = BN < 16 ? BN : 16;
-          const int ncon = c_hi - c_lo + 1;
-#pragma unroll 1
-          for (int c0 = 0; c0 < BN; c0 += CW) {
-            float acc[CW];
-#pragma unroll
-            for (int u = 0; u < CW; ++u) acc[u] = 0.0f;
-#pragma unroll 1
-            for (int cb = 0; cb < ncon; cb += 4) {
-              float4 pv[4][CW / 4];
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                if (cb + j < ncon) {
-                  const int cc = c_lo + cb + j;
-                  const int cs = 2 * cc + (tile == (int)(((long long)cc * a.T / a.G) / KS) ? 0 : 1);
-                  const float4* src = reinterpret_cast<const float4*>(a.partials + (size_t)cs * (kBsRows * BN) +
-                                                                      (size_t)r * BN + c0);
-#pragma unroll
-                  for (int u = 0; u < CW / 4; ++u) pv[j][u] = __ldcg(src + u);
-                }
-              }
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                if (cb + j < ncon) {
-#pragma unroll
-                  for (int u = 0; u < CW / 4; ++u) {
-                    acc[4 * u] += pv[j][u].x; acc[4 * u + 1] += pv[j][u].y;
-                    acc[4 * u + 2] += pv[j][u].z; acc[4 * u + 3] += pv[j][u].w;
-                  }
-                }
-              }
-            }
-            if (live) {
-#pragma unroll
-              for (int u = 0; u < CW; ++u) {
-                const int m = m0 + c0 + u;
-                if (m < a.M) {
-                  if (F32OUT) static_cast<float*>(a.Y)[(size_t)m * a.N + n] = acc[u];
-                  else if (a.tp.world > 0) tp_store(a.tp, (size_t)m, n, __float2bfloat16_rn(acc[u]));
-                  else static_cast<__nv_bfloat16*>(a.Y)[(size_t)m * a.N + n] = __float2bfloat16_rn(acc[u]);
-                }
-              }
-            }
-          }
-          if (warp == kBsEpiWarp0 && lane == 0) a.counters[tile] = 0u;  // leave the workspace zeroed
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");  // s_ticket is reused by the next segment
-      }
       it += ke - kb;
     }
   }
@@ -531,7 +471,75 @@ k_umma_bs(const __grid_constant__ CUtensorMap map_w, const BsArgs a) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM_COLS));
   }
-  if (a.tp.world > 0) tp_finish(a.tp, fault);
+  if (a.tp.world > 0 && !a.fixup) tp_finish(a.tp, fault);
+}
+
+// ---------------------------------------------------------------------------
+// Split-tile fixup.  A tile whose k range CTAs c_lo .. c_hi of k_umma_bs
+// shared (c_hi > c_lo) is summed here: one thread per output quad (one
+// weight row, four activation rows), the contributors' partials added in CTA
+// order starting from zero, the loads of up to 8 contributors in flight
+// before the first add.  Launched right after k_umma_bs with programmatic
+// dependent launch; its wait returns once the GEMM grid has completed, so
+// every partial (and every whole tile's store) has landed.  With a
+// tensor-parallel output this kernel, not the GEMM, ends with tp_finish.
+// ---------------------------------------------------------------------------
+constexpr int kBsMaxSplit = 512;  // split tiles per call: at most G - 1
+struct BsSplitList {
+  int n;
+  int tile[kBsMaxSplit];
+};
+
+template <int BN>
+constexpr int bs_fix_ctas_per_tile() { return (kBsRows * BN / 4 + 255) / 256; }
+
+template <int BN, bool F32OUT>
+__global__ void __launch_bounds__(256) k_bs_fixup(const __grid_constant__ BsSplitList sl, const BsArgs a) {
+  constexpr int PER_TILE = kBsRows * BN / 4;  // float4 outputs of a tile
+  constexpr int CPT = bs_fix_ctas_per_tile<BN>();
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the GEMM grid: partials and whole tiles
+  const int idx = (int)(blockIdx.x % CPT) * 256 + (int)threadIdx.x;  // q 128 + r
+  const int tile = sl.tile[blockIdx.x / CPT];
+  if (idx < PER_TILE) {
+    const int KS = a.KS;
+    const long long t0 = (long long)tile * KS, t1 = t0 + KS - 1;
+    const int c_lo = (int)(((t0 + 1) * a.G - 1) / a.T), c_hi = (int)(((t1 + 1) * a.G - 1) / a.T);
+    const float4* P = reinterpret_cast<const float4*>(a.partials) + idx;
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    constexpr int B = 8;
+#pragma unroll 1
+    for (int c = c_lo; c <= c_hi; c += B) {
+      float4 v[B];
+#pragma unroll
+      for (int u = 0; u < B; ++u)
+        if (c + u <= c_hi) {
+          const int cc = c + u;
+          const int slot = 2 * cc + (tile == (int)(((long long)cc * a.T / a.G) / KS) ? 0 : 1);
+          v[u] = __ldcg(P + (size_t)slot * PER_TILE);
+        }
+#pragma unroll
+      for (int u = 0; u < B; ++u)
+        if (c + u <= c_hi) {
+          acc.x += v[u].x; acc.y += v[u].y; acc.z += v[u].z; acc.w += v[u].w;
+        }
+    }
+    const int q = idx / kBsRows, r = idx % kBsRows;
+    const int n = (tile % a.tiles_n) * kBsRows + r, m0 = (tile / a.tiles_n) * BN + 4 * q;
+    if (n < a.N) {
+      const float y4[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int m = m0 + u;
+        if (m < a.M) {
+          if (F32OUT) static_cast<float*>(a.Y)[(size_t)m * a.N + n] = y4[u];
+          else if (a.tp.world > 0) tp_store(a.tp, (size_t)m, n, __float2bfloat16_rn(y4[u]));
+          else static_cast<__nv_bfloat16*>(a.Y)[(size_t)m * a.N + n] = __float2bfloat16_rn(y4[u]);
+        }
+      }
+    }
+  }
+  if (a.tp.world > 0) tp_finish(a.tp, &g_bs_fault);
 }
 
 // ---------------------------------------------------------------------------
@@ -582,11 +590,34 @@ static BsPlan bs_plan(const qgemm_weights_t* w, int M, int sm_count) {
   p.G = (int)(p.T < sm_count ? p.T : sm_count);
   const size_t xstage = (size_t)2 * p.bn * kBsK + 1024;
   p.x_bytes = (((size_t)((M + p.bn - 1) / p.bn) * p.KS * xstage) + 255) & ~(size_t)255;
-  p.counter_bytes = ws_ticket_bytes(w->N);
+  p.counter_bytes = ws_ticket_bytes(w->N);  // unused here: the fixup kernel needs no tickets
   p.partial_bytes = (((size_t)2 * p.G * kBsRows * p.bn * sizeof(float)) + 255) & ~(size_t)255;
   return p;
 }
-// [tickets | X image | partials]
+// The tiles that stream-K splits: every CTA boundary c T / G (0 < c < G)
+// strictly inside a tile splits it; boundaries rise, so a tile's repeats are
+// adjacent.  Writes up to `cap` tile ids to out (may be null); returns the count.
+static int bs_split_tiles(const BsPlan& p, int* out, int cap) {
+  int n = 0, last = -1;
+  for (int c = 1; c < p.G; ++c) {
+    const long long b = (long long)c * p.T / p.G;
+    if (b % p.KS == 0) continue;
+    const int t = (int)(b / p.KS);
+    if (t == last) continue;
+    if (out && n < cap) out[n] = t;
+    ++n;
+    last = t;
+  }
+  return n;
+}
+
+// Launches of one call: k_xprep_bs, k_umma_bs and, with split tiles, k_bs_fixup.
+int umma_bs_launches(const qgemm_weights_t* w, int M, int sm_count) {
+  if (sm_count <= 0) return 2;
+  return bs_split_tiles(bs_plan(w, M, sm_count), nullptr, 0) > 0 ? 3 : 2;
+}
+
+// [ticket region | X image | partials]
 size_t umma_bs_workspace(const qgemm_weights_t* w, int M, int sm_count) {
   const BsPlan p = bs_plan(w, M, sm_count);
   return p.x_bytes + p.counter_bytes + p.partial_bytes;
@@ -629,7 +660,32 @@ static cudaError_t launch_bs(int bn, const CUtensorMap& mw, const BsArgs& a, cud
 }
 
 // Two launches: k_xprep_bs then k_umma_bs (programmatic dependent launch).
-// ws: umma_bs_workspace bytes, counters zero.
+template <int BN, bool F32>
+static cudaError_t launch_fix_t(const BsSplitList& sl, const BsArgs& a, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(sl.n * bs_fix_ctas_per_tile<BN>()));
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_bs_fixup<BN, F32>, sl, a);
+}
+template <bool F32>
+static cudaError_t launch_fix(int bn, const BsSplitList& sl, const BsArgs& a, cudaStream_t s) {
+  switch (bn) {
+    case 8: return launch_fix_t<8, F32>(sl, a, s);
+    case 16: return launch_fix_t<16, F32>(sl, a, s);
+    case 32: return launch_fix_t<32, F32>(sl, a, s);
+    case 64: return launch_fix_t<64, F32>(sl, a, s);
+    default: return launch_fix_t<128, F32>(sl, a, s);
+  }
+}
+
+// ws: umma_bs_workspace bytes.  A third launch, k_bs_fixup, follows when the
+// stream-K ranges split tiles (bs_split_tiles).
 qgemm_status_t gemm_umma_bs(const qgemm_weights_t* w, const uint16_t* X, int M, void* Y, bool f32, void* ws,
                             int sm_count, cudaStream_t s, const TpOut* tp) {
   if (!umma_bs_supported(w, M)) return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "block-scaled path: unsupported shape");
@@ -645,8 +701,10 @@ qgemm_status_t gemm_umma_bs(const qgemm_weights_t* w, const uint16_t* X, int M, 
           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return fail(QGEMM_ERR_CUDA, "block-scaled path: cuTensorMapEncodeTiled failed");
-  if ((size_t)p.tiles * sizeof(unsigned) > p.counter_bytes)
-    return fail(QGEMM_ERR_WORKSPACE, "block-scaled path: %d tiles exceed the ticket region", p.tiles);
+  BsSplitList sl;  // the fixup kernel's parameter block
+  sl.n = bs_split_tiles(p, sl.tile, kBsMaxSplit);
+  if (sl.n > kBsMaxSplit)
+    return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "block-scaled path: %d split tiles, at most %d", sl.n, kBsMaxSplit);
   uint8_t* img = static_cast<uint8_t*>(ws) + p.counter_bytes;
   const int nrows = (M + p.bn - 1) / p.bn * p.bn;
   {
@@ -667,17 +725,21 @@ qgemm_status_t gemm_umma_bs(const qgemm_weights_t* w, const uint16_t* X, int M, 
   a.scales = static_cast<const uint8_t*>(w->scales);
   a.xbs = img;
   a.Y = Y;
-  a.counters = static_cast<unsigned*>(ws);
   a.partials = reinterpret_cast<float*>(img + p.x_bytes);
   a.T = p.T; a.M = M; a.N = (int)w->N; a.K = (int)w->K;
   a.tiles_n = p.tiles_n; a.KS = p.KS; a.G = p.G;
+  a.fixup = sl.n > 0 ? 1 : 0;
   a.tp = {};
   if (tp) {
     if (f32) return fail(QGEMM_ERR_INVALID_ARG, "block-scaled path: tensor-parallel output is bf16");
     a.tp = *tp;
   }
-  const cudaError_t e = f32 ? launch_bs<true>(p.bn, mw, a, s) : launch_bs<false>(p.bn, mw, a, s);
+  cudaError_t e = f32 ? launch_bs<true>(p.bn, mw, a, s) : launch_bs<false>(p.bn, mw, a, s);
   if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "block-scaled launch: %s", cudaGetErrorString(e));
+  if (sl.n > 0) {
+    e = f32 ? launch_fix<true>(p.bn, sl, a, s) : launch_fix<false>(p.bn, sl, a, s);
+    if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "block-scaled fixup launch: %s", cudaGetErrorString(e));
+  }
   return QGEMM_OK;
 }
 

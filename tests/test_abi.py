@@ -108,9 +108,10 @@ def test_grouped_argument_checks(qg):
 def test_launch_count_mirrors_dispatch(qg):
     """qgemm_launch_count is host-only: which kernel a call uses and how many
     launches it makes (MXFP4 with 9 <= M <= 128, K % 128 == 0 and a 32-byte
-    aligned code array: k_xprep_bs + k_umma_bs; an X-preparation kernel + one
-    GEMM kernel per 16-row block on the decode paths; k_xprep + one tcgen05
-    kernel for M >= 32)."""
+    aligned code array: k_xprep_bs + k_umma_bs, plus k_bs_fixup when the
+    device's stream-K ranges split tiles, which needs its SM count: 2 without
+    a device; an X-preparation kernel + one GEMM kernel per 16-row block on
+    the decode paths; k_xprep + one tcgen05 kernel for M >= 32)."""
     lib = qg.lib()
     kern = qg._i32(0)
 
