@@ -75,6 +75,9 @@ def parse():
     ap.add_argument("--prefill", action="store_true",
                     help="compute-bound table: NVFP4 (28672,8192) and (8192,28672), M in {2048,4096,8192}, "
                          "tcgen05 path vs cuBLAS BF16 of the same shape")
+    ap.add_argument("--layout", default="checked", choices=["canonical", "checked"],
+                    help="MXFP4 / NVFP4 weights as the reference's bytes, or the same bytes in the "
+                         "scale-checked layout (qgemm_repack; every kernel reads it)")
     ap.add_argument("--moe", default=None, choices=sorted(MOE_STEPS),
                     help="mixture-of-experts decode step: one grouped call vs one call per active expert")
     ap.add_argument("--case", default=None,
@@ -96,6 +99,8 @@ def run_case(args):
     W = torch.randn((N, K), generator=gen, device="cuda").mul_(0.02)
     p = qg.pack(fcode, W)
     del W
+    if args.layout == "checked" and fcode in (qg.MXFP4, qg.NVFP4):
+        p = qg.repack(p)
     X = torch.randn((M, K), generator=gen, device="cuda").to(torch.bfloat16)
     Y = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
     ws = qg.make_workspace(p, M)
@@ -156,8 +161,9 @@ def run_moe(args):
     experts = []
     for _ in range(E):
         W = torch.randn((N, K), generator=gen, device="cuda").mul_(0.02)
-        experts.append(qg.pack_mxfp4(W))
-        del W
+        p = qg.pack_mxfp4(W)
+        experts.append(qg.repack(p) if args.layout == "checked" else p)
+        del W, p
     torch.cuda.empty_cache()
     rows = sum(counts)
     offs = [sum(counts[:e]) for e in range(E)]
@@ -482,7 +488,7 @@ def per_call_table(qg, dev, calls, shards, X, Y, ws, fcode, l2, stream, kernel_o
         p = shards[name]
         wbytes = qg.weight_bytes(fcode, p.N, K)
         rot = max(2, math.ceil(2 * l2 / max(wbytes, 1)))
-        copies = [p] + [qg.Packed(p.format, p.N, p.K, p.data.clone(), p.scales.clone(), p.tensor_scale)
+        copies = [p] + [qg.Packed(p.format, p.N, p.K, p.data.clone(), p.scales.clone(), p.tensor_scale, p.layout)
                         for _ in range(rot - 1)]
         inner = max(rot, 8)
         Xm, Ym, wsm = X[(M, K)], Y[(M, name)], ws[(M, name)]
@@ -670,6 +676,8 @@ def main():
         Wl = W[rank * n_loc:(rank + 1) * n_loc].contiguous()
         del W
         shards[name] = qg.pack(fcode, Wl)
+        if args.layout == "checked" and fcode in (qg.MXFP4, qg.NVFP4):
+            shards[name] = qg.repack(shards[name])
         del Wl
         torch.cuda.empty_cache()
     Kset = sorted({K for _, _, K in layers})
@@ -935,6 +943,7 @@ def main():
             "data": "synthetic (seeded N(0,1) X, N(0,0.02) W packed on device)",
             "config": {"workload": args.workload, "format": fmt,
                        "layers": [[n, N, K] for n, N, K in layers], "M": ms,
+                       "layout": args.layout if fmt in ("mxfp4", "nvfp4") else "canonical",
                        "parallelism": f"N-shard x{world}" + (" + all-gather of Y over NVLink peer stores "
                                                               "(qgemm_tp_gemm_w4a16)" if world > 1 else ""),
                        "l2": "cold: step working set 419 MB > 126 MB L2, calls M-major",

@@ -58,12 +58,24 @@ typedef enum {
   QGEMM_FMT_FP8_E4M3 = 6   /* accounting only */
 } qgemm_format_t;
 
+/* Layout of a packed matrix (qgemm_weights_t.layout).
+ *   QGEMM_LAYOUT_CANONICAL      pack.hpp's bytes, as above.
+ *   QGEMM_LAYOUT_SCALE_CHECKED  MXFP4 / NVFP4 only: the same bytes, which
+ *       qgemm_repack has checked to hold no scale byte outside the range the
+ *       decode kernel decodes by exponent arithmetic (MXFP4 E8M0 0x00 and
+ *       0xFF; NVFP4 E4M3 zero, subnormal and NaN).  The TMA-fed decode
+ *       kernel then skips its per-chunk search for such bytes; every other
+ *       kernel reads the bytes as canonical.  Describing weights that hold
+ *       such bytes with this layout gives unspecified values in the outputs
+ *       their blocks reach. */
+typedef enum { QGEMM_LAYOUT_CANONICAL = 0, QGEMM_LAYOUT_SCALE_CHECKED = 1 } qgemm_layout_t;
+
 /* A packed weight matrix resident in device memory.  Replaces the reference's
  * PackedMxfp4 / PackedNvfp4 / PackedInt4 containers (pack.hpp:396-417), whose
  * std::vector members become device pointers of the same length and layout. */
 typedef struct {
   int32_t format;          /* qgemm_format_t (4-bit members only)           */
-  int32_t reserved;        /* must be 0                                      */
+  int32_t layout;          /* qgemm_layout_t (0 = the reference's bytes)     */
   size_t N, K;             /* W is [N, K]                                    */
   const uint8_t* data;     /* N*K/2 bytes                                    */
   const void* scales;      /* MXFP4/NVFP4: uint8 [N*K/blk]; INT4: uint16 bits */
@@ -111,6 +123,40 @@ qgemm_status_t qgemm_dequant(const qgemm_weights_t* w, float* out, void* stream)
  *       3 float_to_fp16_bits -> uint16.                                      */
 qgemm_status_t qgemm_codec_encode(int32_t kind, const float* in, void* out,
                                   size_t n, void* stream);
+
+/* Code-level packers (pack.hpp:611-674): already-quantised codes into the
+ * canonical layout, and back.  MXFP4 / NVFP4: codes are uint8 E2M1 codes
+ * (the low 4 bits are packed, as pack_nibble masks them) and scales_in the
+ * raw E8M0 / E4M3 scale bytes, copied unchanged (pack_mxfp4_codes,
+ * pack_nvfp4_codes; an NVFP4 tensor scale is carried in qgemm_weights_t).
+ * INT4: codes are int32 values clamped to [-8, 7] (int4_to_nibble) and
+ * scales_in FP32 group scales, stored as FP16 bits (float_to_fp16_bits,
+ * pack_int4_codes).  Unpacking returns the uint8 nibbles (unpack_e2m1_codes)
+ * or the int32 signed values (unpack_int4_codes).  N*K must be even and K
+ * divisible by the format's block, or QGEMM_ERR_INVALID_ARG, as the
+ * reference throws (pack.hpp:113-139).  Device pointers, stream-ordered. */
+qgemm_status_t qgemm_pack_codes(int32_t format, const void* codes, const void* scales_in,
+                                size_t N, size_t K, uint8_t* data, void* scales, void* stream);
+qgemm_status_t qgemm_unpack_codes(int32_t format, const uint8_t* data, size_t N, size_t K,
+                                  void* codes, void* stream);
+
+/* ---- layouts: the kernel-optimal layout as an offline transform ----------
+ * The reference plans a kernel-optimal repacked layout derived from the
+ * dequantisation sequence, with the canonical bytes as the parity format
+ * (docs/D1_LAYOUT_DERIVATION.md:17-52).  Here it is
+ * QGEMM_LAYOUT_SCALE_CHECKED (above).  qgemm_layout_sizes gives the buffer
+ * sizes of a layout; qgemm_repack writes canonical weights (src->layout 0)
+ * in `layout` (for the scale-checked layout it scans the scales, waits for
+ * `stream`, and returns QGEMM_ERR_INVALID_ARG if a byte is outside the fast
+ * range: such weights stay canonical); qgemm_unpack writes the canonical
+ * bytes of weights in any layout.  The outputs may alias the source's
+ * arrays (the bytes are then not copied).  Device pointers. */
+qgemm_status_t qgemm_layout_sizes(int32_t format, int32_t layout, size_t N, size_t K,
+                                  size_t* data_bytes, size_t* scale_bytes);
+qgemm_status_t qgemm_repack(const qgemm_weights_t* src, int32_t layout, uint8_t* data,
+                            void* scales, void* stream);
+qgemm_status_t qgemm_unpack(const qgemm_weights_t* src, uint8_t* data, void* scales,
+                            void* stream);
 
 /* ---- GEMM ------------------------------------------------------------------
  * Workspace: scratch the kernels use for split-K partial sums, tile tickets

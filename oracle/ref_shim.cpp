@@ -147,4 +147,39 @@ int ref_w4a16_gemm(int fmt, const uint8_t* data, const void* scales, size_t N, s
   return 0;
 }
 
+// Code-level packers and unpackers (pack.hpp:611-674); 0 on success, -1 when
+// the reference throws.
+int ref_pack_int4_codes(const int* q, const float* sc, size_t N, size_t K, int g, uint8_t* data, uint16_t* scales) {
+  try {
+    PackedInt4 p = pack_int4_codes(q, sc, N, K, g);
+    std::memcpy(data, p.data.data(), p.data.size());
+    std::memcpy(scales, p.scales.data(), p.scales.size() * 2);
+    return 0;
+  } catch (const std::invalid_argument&) { return -1; }
+}
+int ref_pack_mxfp4_codes(const uint8_t* c, const uint8_t* sb, size_t N, size_t K, uint8_t* data, uint8_t* scales) {
+  try {
+    PackedMxfp4 p = pack_mxfp4_codes(c, sb, N, K);
+    std::memcpy(data, p.data.data(), p.data.size());
+    std::memcpy(scales, p.scales.data(), p.scales.size());
+    return 0;
+  } catch (const std::invalid_argument&) { return -1; }
+}
+int ref_pack_nvfp4_codes(const uint8_t* c, const uint8_t* sb, size_t N, size_t K, float ts, uint8_t* data,
+                         uint8_t* scales) {
+  try {
+    PackedNvfp4 p = pack_nvfp4_codes(c, sb, N, K, ts);
+    std::memcpy(data, p.data.data(), p.data.size());
+    std::memcpy(scales, p.scales.data(), p.scales.size());
+    return 0;
+  } catch (const std::invalid_argument&) { return -1; }
+}
+void ref_unpack_int4_codes(const uint8_t* d, size_t N, size_t K, int* q) {
+  PackedInt4 p;
+  p.N = N; p.K = K;
+  p.data.assign(d, d + N * K / 2);
+  unpack_int4_codes(p, q);
+}
+void ref_unpack_e2m1_codes(const uint8_t* d, size_t N, size_t K, uint8_t* c) { unpack_e2m1_codes(d, N, K, c); }
+
 }  // extern "C"

@@ -42,7 +42,7 @@ _vp, _sz, _i32, _f32, _u16p = C.c_void_p, C.c_size_t, C.c_int32, C.c_float, C.c_
 
 
 class _Weights(C.Structure):
-    _fields_ = [("format", _i32), ("reserved", _i32), ("N", _sz), ("K", _sz),
+    _fields_ = [("format", _i32), ("layout", _i32), ("N", _sz), ("K", _sz),
                 ("data", _vp), ("scales", _vp), ("tensor_scale", _f32)]
 
 
@@ -67,6 +67,11 @@ _sig("qgemm_pack_int4", _i32, [_vp, _sz, _sz, _i32, _vp, _vp, _vp])
 _sig("qgemm_nvfp4_tensor_scale", _i32, [_vp, _sz, _vp, _vp])
 _sig("qgemm_dequant", _i32, [C.POINTER(_Weights), _vp, _vp])
 _sig("qgemm_codec_encode", _i32, [_i32, _vp, _vp, _sz, _vp])
+_sig("qgemm_pack_codes", _i32, [_i32, _vp, _vp, _sz, _sz, _vp, _vp, _vp])
+_sig("qgemm_unpack_codes", _i32, [_i32, _vp, _sz, _sz, _vp, _vp])
+_sig("qgemm_layout_sizes", _i32, [_i32, _i32, _sz, _sz, C.POINTER(_sz), C.POINTER(_sz)])
+_sig("qgemm_repack", _i32, [C.POINTER(_Weights), _i32, _vp, _vp, _vp])
+_sig("qgemm_unpack", _i32, [C.POINTER(_Weights), _vp, _vp, _vp])
 _sig("qgemm_workspace_size", _sz, [C.POINTER(_Weights), _i32])
 _sig("qgemm_launch_count", _i32, [C.POINTER(_Weights), _i32, C.POINTER(_i32)])
 _sig("qgemm_workspace_init", _i32, [_vp, _sz, _vp])
@@ -164,21 +169,23 @@ class Packed:
     data: torch.Tensor
     scales: torch.Tensor
     tensor_scale: float = 1.0
+    layout: int = 0  # CANONICAL or SCALE_CHECKED (include/qgemm_b200.h)
 
     @property
     def group(self) -> int:
         return {MXFP4: 32, NVFP4: 16, INT4_G128: 128, INT4_G64: 64}[self.format]
 
     def desc(self) -> _Weights:
-        return _Weights(self.format, 0, self.N, self.K, self.data.data_ptr(),
+        return _Weights(self.format, self.layout, self.N, self.K, self.data.data_ptr(),
                         self.scales.data_ptr(), float(self.tensor_scale))
 
     def shard_rows(self, n0: int, n1: int) -> "Packed":
-        """Rows [n0, n1) as a view: contiguous slices of data and scales."""
+        """Rows [n0, n1) as a view: contiguous slices of data and scales, in
+        the same layout (a row subset of checked scales is checked)."""
         bpr = self.K // 2
         spr = self.K // self.group
         return Packed(self.format, n1 - n0, self.K, self.data[n0 * bpr:n1 * bpr],
-                      self.scales[n0 * spr:n1 * spr], self.tensor_scale)
+                      self.scales[n0 * spr:n1 * spr], self.tensor_scale, self.layout)
 
 
 def _alloc_packed(fmt: int, N: int, K: int, device) -> tuple[torch.Tensor, torch.Tensor]:
@@ -277,6 +284,62 @@ def dequant(p: Packed, stream=None) -> torch.Tensor:
 
 
 dequant_mxfp4 = dequant_nvfp4 = dequant_int4 = dequant
+
+
+def pack_codes(fmt: int, codes: torch.Tensor, scales: torch.Tensor, N: int, K: int,
+               tensor_scale: float = 1.0, stream=None) -> Packed:
+    """Already-quantised codes to the canonical layout (pack.hpp:611-665):
+    FP4 formats take uint8 E2M1 codes [N*K] and uint8 scale bytes; INT4 takes
+    int32 codes in [-8, 7] (clamped) and float32 group scales."""
+    int4 = fmt in (INT4_G128, INT4_G64)
+    want_c, want_s = (torch.int32, torch.float32) if int4 else (torch.uint8, torch.uint8)
+    if codes.dtype != want_c or scales.dtype != want_s:
+        raise ValueError(f"pack_codes: codes must be {want_c}, scales {want_s}")
+    codes, scales = codes.contiguous(), scales.contiguous()
+    data, sc = _alloc_packed(fmt, N, K, codes.device)
+    _check(_lib.qgemm_pack_codes(fmt, _ptr(codes), _ptr(scales), N, K, _ptr(data), _ptr(sc), _stream(stream)),
+           "pack_codes")
+    return Packed(fmt, N, K, data, sc, tensor_scale if fmt == NVFP4 else 1.0)
+
+
+def unpack_codes(p: Packed, stream=None) -> torch.Tensor:
+    """The packed codes back (pack.hpp:667-682): uint8 E2M1 codes, or int32
+    INT4 values, [N*K]."""
+    int4 = p.format in (INT4_G128, INT4_G64)
+    out = torch.empty(p.N * p.K, dtype=torch.int32 if int4 else torch.uint8, device=p.data.device)
+    _check(_lib.qgemm_unpack_codes(p.format, _ptr(p.data), p.N, p.K, _ptr(out), _stream(stream)), "unpack_codes")
+    return out
+
+
+# ---- layouts (the kernel-optimal layout as an offline transform) --------------
+
+CANONICAL, SCALE_CHECKED = 0, 1
+
+
+def layout_sizes(fmt: int, layout: int, N: int, K: int) -> tuple[int, int]:
+    d, s = _sz(0), _sz(0)
+    _check(_lib.qgemm_layout_sizes(fmt, layout, N, K, C.byref(d), C.byref(s)), "layout_sizes")
+    return d.value, s.value
+
+
+def repack(p: Packed, layout: int = SCALE_CHECKED, stream=None) -> Packed:
+    """Canonical weights in `layout`.  The scale-checked layout keeps the
+    bytes (shared with p, nothing is copied) once a scan of the scales finds
+    none outside the decode kernel's fast range; ValueError otherwise (such
+    weights stay canonical).  Waits for the stream."""
+    if p.layout != CANONICAL:
+        raise ValueError("repack: source must be canonical")
+    d = p.desc()
+    _check(_lib.qgemm_repack(C.byref(d), layout, _ptr(p.data), _ptr(p.scales), _stream(stream)), "repack")
+    return Packed(p.format, p.N, p.K, p.data, p.scales, p.tensor_scale, layout)
+
+
+def unpack(p: Packed, stream=None) -> Packed:
+    """The canonical bytes of p (any layout), in new buffers."""
+    data, sc = _alloc_packed(p.format, p.N, p.K, p.data.device)
+    d = p.desc()
+    _check(_lib.qgemm_unpack(C.byref(d), _ptr(data), _ptr(sc), _stream(stream)), "unpack")
+    return Packed(p.format, p.N, p.K, data, sc, p.tensor_scale, CANONICAL)
 
 
 def codec_encode(kind: str, x: torch.Tensor, stream=None) -> torch.Tensor:

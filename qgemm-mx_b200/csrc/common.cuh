@@ -62,6 +62,15 @@ qgemm_status_t device_props(DevProps* p);
 // calls included, can share one workspace.
 size_t ws_ticket_bytes(size_t N);
 
+// Layout checks shared by the entry points (null if fine, else a message).
+inline const char* layout_error(const qgemm_weights_t* w) {
+  if (w->layout == QGEMM_LAYOUT_CANONICAL) return nullptr;
+  if (w->layout != QGEMM_LAYOUT_SCALE_CHECKED) return "unknown layout";
+  if (w->format != QGEMM_FMT_MXFP4 && w->format != QGEMM_FMT_NVFP4)
+    return "the scale-checked layout is MXFP4 / NVFP4 only";
+  return nullptr;
+}
+
 // ---------------------------------------------------------------------------
 // Bit helpers
 // ---------------------------------------------------------------------------

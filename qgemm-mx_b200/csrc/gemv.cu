@@ -689,7 +689,7 @@ qgemm_status_t gemm_decode_ex(const qgemm_weights_t* w, const uint16_t* X, int M
   if (!w || !X || (!Y && !tp)) return fail(QGEMM_ERR_INVALID_ARG, "gemm: null pointer");
   if (M < 1) return fail(QGEMM_ERR_INVALID_ARG, "gemm: M must be >= 1");
   if (!w->data || !w->scales) return fail(QGEMM_ERR_INVALID_ARG, "gemm: null weight pointer");
-  if (w->reserved != 0) return fail(QGEMM_ERR_INVALID_ARG, "gemm: reserved field must be 0");
+  if (const char* le = layout_error(w)) return fail(QGEMM_ERR_INVALID_ARG, "gemm: %s", le);
   if (w->format == QGEMM_FMT_NVFP4 && !std::isfinite(w->tensor_scale))
     return fail(QGEMM_ERR_INVALID_ARG, "gemm: NVFP4 tensor_scale must be finite");
   GemvPlan p;
@@ -926,7 +926,7 @@ extern "C" qgemm_status_t qgemm_gemm_w4a16_noalloc(const qgemm_weights_t* w, con
   if (!w || !X || !Y) return fail(QGEMM_ERR_INVALID_ARG, "gemm_noalloc: null pointer");
   if (M < 1) return fail(QGEMM_ERR_INVALID_ARG, "gemm_noalloc: M must be >= 1");
   if (!w->data || !w->scales) return fail(QGEMM_ERR_INVALID_ARG, "gemm_noalloc: null weight pointer");
-  if (w->reserved != 0) return fail(QGEMM_ERR_INVALID_ARG, "gemm_noalloc: reserved field must be 0");
+  if (const char* le = layout_error(w)) return fail(QGEMM_ERR_INVALID_ARG, "gemm_noalloc: %s", le);
   if (w->format == QGEMM_FMT_NVFP4 && !std::isfinite(w->tensor_scale))
     return fail(QGEMM_ERR_INVALID_ARG, "gemm_noalloc: NVFP4 tensor_scale must be finite");
   LdgLayout L;
@@ -1002,6 +1002,7 @@ static qgemm_status_t grouped_gemm(const qgemm_weights_t* w, int E, const uint16
     const qgemm_weights_t& we = w[e];
     if (we.format != w[0].format || we.N != w[0].N || we.K != w[0].K)
       return fail(QGEMM_ERR_INVALID_ARG, "grouped_gemm: expert %d differs from expert 0 in format or shape", e);
+    if (const char* le = layout_error(&we)) return fail(QGEMM_ERR_INVALID_ARG, "grouped_gemm: expert %d: %s", e, le);
     if (M[e] < 0 || offs[e] < 0)
       return fail(QGEMM_ERR_INVALID_ARG, "grouped_gemm: expert %d has M %d, row offset %lld", e, M[e],
                   (long long)offs[e]);
@@ -1028,7 +1029,7 @@ static qgemm_status_t grouped_gemm(const qgemm_weights_t* w, int E, const uint16
   for (int e = 0; e < E; ++e) {
     if (M[e] == 0) continue;
     const qgemm_weights_t* we = &w[e];
-    if (!we->data || !we->scales || we->reserved != 0 ||
+    if (!we->data || !we->scales || layout_error(we) ||
         (we->format == QGEMM_FMT_NVFP4 && !std::isfinite(we->tensor_scale)) || !al16(we->data))
       return fail(QGEMM_ERR_INVALID_ARG, "grouped_gemm: expert %d: null or misaligned weights, or bad tensor_scale", e);
     if (grouped_fused(we, M[e]) && al16(X)) {

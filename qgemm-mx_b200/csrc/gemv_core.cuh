@@ -150,7 +150,14 @@ __device__ __forceinline__ uint32_t f16x2_of(float f) {
 //   cs[r][h]     their scale bits for the chunk
 //   cx[t][16]    the X fragment words of activation rows 8t + g
 // FMT: 0 MXFP4, 1 NVFP4, 2 INT4 g128, 3 INT4 g64.
-template <int FMT, int R, int NT>
+// SCALES (FP4 formats): how block scales are decoded.
+//   kScalesCheck  fast decode, and the exact decoder for the whole warp when
+//                 the chunk holds a byte the fast decode does not cover
+//                 (found by a per-chunk search);
+//   kScalesFast   fast decode only: the weights are in the scale-checked
+//                 layout, so no such byte occurs.
+constexpr int kScalesCheck = 0, kScalesFast = 1;
+template <int FMT, int R, int NT, int SCALES = kScalesCheck>
 __device__ __forceinline__ void chunk_mma(float (&acc)[R][NT][4], const uint32_t (&cw)[R][2][4],
                                           const uint32_t (&cs)[R][2], const uint32_t (&cx)[NT][16]) {
   if constexpr (FMT == 0) {
@@ -164,11 +171,11 @@ __device__ __forceinline__ void chunk_mma(float (&acc)[R][NT][4], const uint32_t
     for (int r = 0; r < R; ++r)
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        special |= has_00_or_ff(cs[r][h]);
+        if (SCALES == kScalesCheck) special |= has_00_or_ff(cs[r][h]);
 #pragma unroll
         for (int b = 0; b < 4; ++b) sc[r][h][b] = e8m0_fast(cs[r][h], b);
       }
-    if (__any_sync(0xFFFFFFFFu, special)) {
+    if (SCALES == kScalesCheck && __any_sync(0xFFFFFFFFu, special)) {
 #pragma unroll
       for (int r = 0; r < R; ++r)
 #pragma unroll
@@ -208,7 +215,7 @@ __device__ __forceinline__ void chunk_mma(float (&acc)[R][NT][4], const uint32_t
     for (int r = 0; r < R; ++r)
 #pragma unroll
       for (int h = 0; h < 2; ++h) slow |= !e4m3x2_to_f16x2_fast(cs[r][h], sw[r][h][0], sw[r][h][1]);
-    if (__any_sync(0xFFFFFFFFu, slow)) {
+    if (SCALES == kScalesCheck && __any_sync(0xFFFFFFFFu, slow)) {
 #pragma unroll
       for (int r = 0; r < R; ++r)
 #pragma unroll

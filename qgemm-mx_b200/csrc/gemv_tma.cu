@@ -53,6 +53,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstring>
+#include <type_traits>
 
 #include "common.cuh"
 #include "gemv_core.cuh"
@@ -183,7 +184,58 @@ __global__ void __launch_bounds__(kXuWarps * 32) k_xprep_units(const __grid_cons
   if (lane == 0) reinterpret_cast<float*>(unit + mpad * (kGtUnitK * 2))[m] = f;
 }
 
-template <int FMT, int NT, int RPW, int UG, bool F32OUT, int MAXE>
+// One consumer warp's pass over a unit's two 128-k chunks in the stage
+// (codes W, X image, scales SC): its RPW 16-row groups' sums into accu.
+template <int FMT, int NT, int RPW, int SB, int SCM>
+__device__ __forceinline__ void gt_unit_pass(float (&accu)[RPW][NT][4], const uint8_t* W, const uint8_t* X,
+                                             const uint8_t* SC, int wq, int lane) {
+  const int g = lane >> 2, j = lane & 3;
+  const uint32_t sw = (uint32_t)(g & 7);  // every row this lane touches is g mod 8
+#pragma unroll
+  for (int r = 0; r < RPW; ++r)
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) accu[r][t][e] = 0.0f;
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {  // the unit's two 128-k chunks
+    uint32_t cw[RPW][2][4], cs[RPW][2], cx[NT][16];
+#pragma unroll
+    for (int r = 0; r < RPW; ++r)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int row = 16 * (RPW * wq + r) + g + 8 * h;
+        const uint8_t* wr = W + row * 128;
+        if (FMT == 0) {  // 4 bytes of each of the chunk's 4 blocks
+#pragma unroll
+          for (int b = 0; b < 4; ++b)
+            cw[r][h][b] = *reinterpret_cast<const uint32_t*>(wr + ((((uint32_t)(4 * c + b)) ^ sw) << 4) + 4 * j);
+          cs[r][h] = *reinterpret_cast<const uint32_t*>(SC + row * SB + 4 * c);
+        } else {         // 16 contiguous bytes
+          const uint4 v = *reinterpret_cast<const uint4*>(wr + ((((uint32_t)(4 * c + j)) ^ sw) << 4));
+          cw[r][h][0] = v.x; cw[r][h][1] = v.y; cw[r][h][2] = v.z; cw[r][h][3] = v.w;
+          cs[r][h] = *reinterpret_cast<const uint16_t*>(SC + row * SB + 8 * c + 2 * j);
+        }
+      }
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const int m = 8 * t + g;
+      const uint8_t* xr = X + m * (kGtUnitK * 2);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int idx = (FMT == 0) ? 16 * c + 4 * q + j : 16 * c + 4 * j + q;  // 8-f16 chunk of the unit
+        const uint4 v = *reinterpret_cast<const uint4*>(xr + xg_pos(FMT, idx, m) * 16);
+        cx[t][4 * q] = v.x; cx[t][4 * q + 1] = v.y; cx[t][4 * q + 2] = v.z; cx[t][4 * q + 3] = v.w;
+      }
+    }
+    chunk_mma<FMT, RPW, NT, SCM>(accu, cw, cs, cx);
+  }
+}
+
+// FAST: every problem's weights are in the scale-checked layout (no scale
+// byte needs the exact decoder), so the consumers decode scales without the
+// per-chunk search for such bytes.
+template <int FMT, int NT, int RPW, int UG, bool F32OUT, int MAXE, bool FAST>
 __global__ void __launch_bounds__(GtCfg<FMT, NT, RPW, UG>::THREADS, 1)
 k_gemv_tma(const __grid_constant__ GtGroup<MAXE> pg, const GtArgs a) {
   using C = GtCfg<FMT, NT, RPW, UG>;
@@ -292,7 +344,6 @@ k_gemv_tma(const __grid_constant__ GtGroup<MAXE> pg, const GtArgs a) {
     const int ug = cons / WPG;                      // unit group: the units i with i % UG == ug
     const int wq = cons % WPG;                      // weight rows [16 RPW wq, 16 RPW (wq + 1)) of a unit
     const int g = lane >> 2, j = lane & 3;
-    const uint32_t sw = (uint32_t)(g & 7);         // every row this lane touches is g mod 8
     // (no programmatic-launch wait here: every consumer step depends on a
     // unit whose X the producers copied after theirs)
 
@@ -408,40 +459,7 @@ k_gemv_tma(const __grid_constant__ GtGroup<MAXE> pg, const GtArgs a) {
           const uint8_t* W = gbase + W_off(s);
           const uint8_t* X = gbase + X_off(s);
           const uint8_t* SC = gbase + S_off(s);
-          zero(accu);
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {  // the unit's two 128-k chunks
-            uint32_t cw[RPW][2][4], cs[RPW][2], cx[NT][16];
-#pragma unroll
-            for (int r = 0; r < RPW; ++r)
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const int row = 16 * grp(r) + g + 8 * h;
-                const uint8_t* wr = W + row * 128;
-                if (FMT == 0) {  // 4 bytes of each of the chunk's 4 blocks
-#pragma unroll
-                  for (int b = 0; b < 4; ++b)
-                    cw[r][h][b] = *reinterpret_cast<const uint32_t*>(wr + ((((uint32_t)(4 * c + b)) ^ sw) << 4) + 4 * j);
-                  cs[r][h] = *reinterpret_cast<const uint32_t*>(SC + row * C::SB + 4 * c);
-                } else {         // 16 contiguous bytes
-                  const uint4 v = *reinterpret_cast<const uint4*>(wr + ((((uint32_t)(4 * c + j)) ^ sw) << 4));
-                  cw[r][h][0] = v.x; cw[r][h][1] = v.y; cw[r][h][2] = v.z; cw[r][h][3] = v.w;
-                  cs[r][h] = *reinterpret_cast<const uint16_t*>(SC + row * C::SB + 8 * c + 2 * j);
-                }
-              }
-#pragma unroll
-            for (int t = 0; t < NT; ++t) {
-              const int m = 8 * t + g;
-              const uint8_t* xr = X + m * (kGtUnitK * 2);
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const int idx = (FMT == 0) ? 16 * c + 4 * q + j : 16 * c + 4 * j + q;  // 8-f16 chunk of the unit
-                const uint4 v = *reinterpret_cast<const uint4*>(xr + xg_pos(FMT, idx, m) * 16);
-                cx[t][4 * q] = v.x; cx[t][4 * q + 1] = v.y; cx[t][4 * q + 2] = v.z; cx[t][4 * q + 3] = v.w;
-              }
-            }
-            chunk_mma<FMT, RPW, NT>(accu, cw, cs, cx);
-          }
+          gt_unit_pass<FMT, NT, RPW, C::SB, FAST ? kScalesFast : kScalesCheck>(accu, W, X, SC, wq, lane);
           // acc += unit sums * 2^s of their activation rows (exact scaling)
           const float* XF = reinterpret_cast<const float*>(gbase + XF_off(s));
 #pragma unroll
@@ -554,7 +572,7 @@ constexpr int gt_rpw() { return NT == 1 ? 2 : 1; }
 template <int NT>
 constexpr int gt_ug() { return NT == 1 ? 3 : 1; }
 
-template <int FMT, int NT, bool F32, int MAXE>
+template <int FMT, int NT, bool F32, int MAXE, bool FAST>
 static cudaError_t launch_gt_t(const GtGroup<MAXE>& g, const GtArgs& a, cudaStream_t s) {
   constexpr int BYTES = GtCfg<FMT, NT, gt_rpw<NT>(), gt_ug<NT>()>::BYTES;
   static bool attr[64] = {false};
@@ -563,7 +581,7 @@ static cudaError_t launch_gt_t(const GtGroup<MAXE>& g, const GtArgs& a, cudaStre
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr[dev]) {
-    e = cudaFuncSetAttribute(k_gemv_tma<FMT, NT, gt_rpw<NT>(), gt_ug<NT>(), F32, MAXE>,
+    e = cudaFuncSetAttribute(k_gemv_tma<FMT, NT, gt_rpw<NT>(), gt_ug<NT>(), F32, MAXE, FAST>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, BYTES);
     if (e != cudaSuccess) return e;
     attr[dev] = true;
@@ -578,17 +596,27 @@ static cudaError_t launch_gt_t(const GtGroup<MAXE>& g, const GtArgs& a, cudaStre
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k_gemv_tma<FMT, NT, gt_rpw<NT>(), gt_ug<NT>(), F32, MAXE>, g, a);
+  return cudaLaunchKernelEx(&cfg, k_gemv_tma<FMT, NT, gt_rpw<NT>(), gt_ug<NT>(), F32, MAXE, FAST>, g, a);
 }
 
-template <int MAXE>
-static cudaError_t launch_gt(int fmt, int nt, bool f32, const GtGroup<MAXE>& g, const GtArgs& a, cudaStream_t s) {
-  if (fmt == QGEMM_FMT_MXFP4) {
-    if (nt == 1) return f32 ? launch_gt_t<0, 1, true, MAXE>(g, a, s) : launch_gt_t<0, 1, false, MAXE>(g, a, s);
-    return f32 ? launch_gt_t<0, 2, true, MAXE>(g, a, s) : launch_gt_t<0, 2, false, MAXE>(g, a, s);
+template <int FMT, int NT, int MAXE, bool FAST>
+static cudaError_t launch_gt_f(bool f32, const GtGroup<MAXE>& g, const GtArgs& a, cudaStream_t s) {
+  if constexpr (MAXE == 1) {
+    if (f32) return launch_gt_t<FMT, NT, true, MAXE, FAST>(g, a, s);
   }
-  if (nt == 1) return f32 ? launch_gt_t<1, 1, true, MAXE>(g, a, s) : launch_gt_t<1, 1, false, MAXE>(g, a, s);
-  return f32 ? launch_gt_t<1, 2, true, MAXE>(g, a, s) : launch_gt_t<1, 2, false, MAXE>(g, a, s);
+  return launch_gt_t<FMT, NT, false, MAXE, FAST>(g, a, s);  // grouped calls: bf16 output only
+}
+template <int MAXE, bool FAST>
+static cudaError_t launch_gt_l(int fmt, int nt, bool f32, const GtGroup<MAXE>& g, const GtArgs& a, cudaStream_t s) {
+  if (fmt == QGEMM_FMT_MXFP4)
+    return nt == 1 ? launch_gt_f<0, 1, MAXE, FAST>(f32, g, a, s) : launch_gt_f<0, 2, MAXE, FAST>(f32, g, a, s);
+  return nt == 1 ? launch_gt_f<1, 1, MAXE, FAST>(f32, g, a, s) : launch_gt_f<1, 2, MAXE, FAST>(f32, g, a, s);
+}
+// fast: every problem of the launch is in the scale-checked layout
+template <int MAXE>
+static cudaError_t launch_gt(int fmt, int nt, bool f32, bool fast, const GtGroup<MAXE>& g, const GtArgs& a,
+                             cudaStream_t s) {
+  return fast ? launch_gt_l<MAXE, true>(fmt, nt, f32, g, a, s) : launch_gt_l<MAXE, false>(fmt, nt, f32, g, a, s);
 }
 
 template <int MAXE>
@@ -639,7 +667,7 @@ qgemm_status_t gemm_gemv_tma(const qgemm_weights_t* w, const uint16_t* X, int mb
   a.KS = p.KS; a.G = p.G;
   a.tp = {};
   if (tp) a.tp = *tp;
-  e = launch_gt<1>(w->format, p.nt, f32, g, a, s);
+  e = launch_gt<1>(w->format, p.nt, f32, w->layout == QGEMM_LAYOUT_SCALE_CHECKED, g, a, s);
   if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "TMA decode launch: %s", cudaGetErrorString(e));
   return QGEMM_OK;
 }
@@ -691,7 +719,9 @@ qgemm_status_t gemm_gemv_tma_group(const qgemm_weights_t* const* w, const int* M
   a.T = p.T; a.N = (int)w[0]->N; a.K = (int)w[0]->K; a.ldy = (int)w[0]->N; a.tiles = p.tiles;
   a.KS = p.KS; a.G = p.G;
   a.tp = {};
-  e = launch_gt<kGtMaxExperts>(w[0]->format, p.nt, false, g, a, s);
+  bool fast = true;  // the checked decode only when every problem's scales are checked
+  for (int q = 0; q < n; ++q) fast = fast && w[q]->layout == QGEMM_LAYOUT_SCALE_CHECKED;
+  e = launch_gt<kGtMaxExperts>(w[0]->format, p.nt, false, fast, g, a, s);
   if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "grouped decode launch: %s", cudaGetErrorString(e));
   return QGEMM_OK;
 }

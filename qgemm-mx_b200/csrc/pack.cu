@@ -323,6 +323,55 @@ __global__ void k_codec(int kind, const float* __restrict__ in, void* __restrict
   }
 }
 
+// ---------------------------------------------------------------------------
+// Code-level packing (pack.hpp:611-674): already-quantised codes to the
+// canonical layout and back.  One thread per output byte pair of codes;
+// even linear index in the low nibble (pack_nibble, pack.hpp:159-168).
+// FP4 codes keep their low 4 bits; INT4 codes are clamped to [-8, 7] and
+// stored two's complement (int4_to_nibble, pack.hpp:386-390).
+// ---------------------------------------------------------------------------
+
+__global__ void k_pack_codes(int int4, const void* __restrict__ codes, uint8_t* __restrict__ data, size_t nbytes) {
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < nbytes; i += stride) {
+    uint32_t lo, hi;
+    if (int4) {
+      const int* q = static_cast<const int*>(codes);
+      const int a = min(max(q[2 * i], -8), 7), b = min(max(q[2 * i + 1], -8), 7);
+      lo = (uint32_t)a & 0xFu;
+      hi = (uint32_t)b & 0xFu;
+    } else {
+      const uint8_t* c = static_cast<const uint8_t*>(codes);
+      lo = c[2 * i] & 0xFu;
+      hi = c[2 * i + 1] & 0xFu;
+    }
+    data[i] = (uint8_t)(lo | (hi << 4));
+  }
+}
+
+__global__ void k_unpack_codes(int int4, const uint8_t* __restrict__ data, void* __restrict__ codes, size_t nbytes) {
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < nbytes; i += stride) {
+    const uint32_t b = data[i];
+    if (int4) {
+      int* q = static_cast<int*>(codes);
+      q[2 * i] = int4_from_nibble(b & 0xFu);  // int4_from_nibble, pack.hpp:381-384
+      q[2 * i + 1] = int4_from_nibble(b >> 4);
+    } else {
+      uint8_t* c = static_cast<uint8_t*>(codes);
+      c[2 * i] = (uint8_t)(b & 0xFu);
+      c[2 * i + 1] = (uint8_t)(b >> 4);
+    }
+  }
+}
+
+// FP32 group scales to FP16 bits (float_to_fp16_bits, pack.hpp:213-258).
+__global__ void k_scales_fp16(const float* __restrict__ in, uint16_t* __restrict__ out, size_t n) {
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    out[i] = (uint16_t)float_to_fp16_bits(in[i]);
+}
+
 static unsigned grid_for(size_t work, int per_block, int sms) {
   size_t g = (work + per_block - 1) / per_block;
   const size_t cap = (size_t)sms * 8;
@@ -467,6 +516,60 @@ qgemm_status_t qgemm_dequant(const qgemm_weights_t* w, float* out, void* stream)
   if (w->format == QGEMM_FMT_MXFP4) k_dequant<0><<<g, 256, 0, s>>>(d32, w->scales, oct, K, 32, 1.0f, out);
   else if (w->format == QGEMM_FMT_NVFP4) k_dequant<1><<<g, 256, 0, s>>>(d32, w->scales, oct, K, 16, w->tensor_scale, out);
   else k_dequant<2><<<g, 256, 0, s>>>(d32, w->scales, oct, K, group, 1.0f, out);
+  QG_LAUNCH_RET();
+  return QGEMM_OK;
+}
+
+// The block size of a 4-bit format, 0 for an unknown format.
+static int format_block(int32_t format) {
+  switch (format) {
+    case QGEMM_FMT_MXFP4: return 32;
+    case QGEMM_FMT_NVFP4: return 16;
+    case QGEMM_FMT_INT4_G128: return 128;
+    case QGEMM_FMT_INT4_G64: return 64;
+    default: return 0;
+  }
+}
+
+qgemm_status_t qgemm_pack_codes(int32_t format, const void* codes, const void* scales_in, size_t N, size_t K,
+                                uint8_t* data, void* scales, void* stream) {
+  const int blk = format_block(format);
+  if (blk == 0) return fail(QGEMM_ERR_INVALID_ARG, "pack_codes: unknown format %d", (int)format);
+  if ((N * K) & 1u) return fail(QGEMM_ERR_INVALID_ARG, "pack_codes: N*K must be even");
+  if (K % (size_t)blk != 0) return fail(QGEMM_ERR_INVALID_ARG, "pack_codes: K must be divisible by %d", blk);
+  if (N * K == 0) return QGEMM_OK;
+  if (!codes || !scales_in || !data || !scales) return fail(QGEMM_ERR_INVALID_ARG, "pack_codes: null pointer");
+  DevProps dp;
+  qgemm_status_t st = device_props(&dp);
+  if (st != QGEMM_OK) return st;
+  cudaStream_t s = as_stream(stream);
+  const bool int4 = blk >= 64;
+  const size_t nbytes = N * K / 2, nscales = N * (K / (size_t)blk);
+  k_pack_codes<<<grid_for(nbytes, 256, dp.sm_count), 256, 0, s>>>(int4 ? 1 : 0, codes, data, nbytes);
+  QG_LAUNCH_RET();
+  if (int4) {
+    k_scales_fp16<<<grid_for(nscales, 256, dp.sm_count), 256, 0, s>>>(static_cast<const float*>(scales_in),
+                                                                      static_cast<uint16_t*>(scales), nscales);
+    QG_LAUNCH_RET();
+  } else {
+    QG_CUDA_RET(cudaMemcpyAsync(scales, scales_in, nscales, cudaMemcpyDeviceToDevice, s));
+  }
+  return QGEMM_OK;
+}
+
+qgemm_status_t qgemm_unpack_codes(int32_t format, const uint8_t* data, size_t N, size_t K, void* codes,
+                                  void* stream) {
+  const int blk = format_block(format);
+  if (blk == 0) return fail(QGEMM_ERR_INVALID_ARG, "unpack_codes: unknown format %d", (int)format);
+  if ((N * K) & 1u) return fail(QGEMM_ERR_INVALID_ARG, "unpack_codes: N*K must be even");
+  if (N * K == 0) return QGEMM_OK;
+  if (!data || !codes) return fail(QGEMM_ERR_INVALID_ARG, "unpack_codes: null pointer");
+  DevProps dp;
+  qgemm_status_t st = device_props(&dp);
+  if (st != QGEMM_OK) return st;
+  const size_t nbytes = N * K / 2;
+  k_unpack_codes<<<grid_for(nbytes, 256, dp.sm_count), 256, 0, as_stream(stream)>>>(blk >= 64 ? 1 : 0, data, codes,
+                                                                                      nbytes);
   QG_LAUNCH_RET();
   return QGEMM_OK;
 }

@@ -132,3 +132,69 @@ def test_pack_rejects_like_reference(qg, cuda):
         qg.pack_int4(torch.zeros((4, 96), dtype=torch.float32, device="cuda"), 64)
     with pytest.raises(ValueError):
         qg.pack_nvfp4(torch.zeros((4, 32), dtype=torch.float32, device="cuda"), 0.0)
+
+
+# ---- code-level packers (pack.hpp:611-674) against the reference's own ---------------
+
+def _ref_code_fns(ref):
+    import ctypes as C
+    L = ref.lib
+    vp, sz = C.c_void_p, C.c_size_t
+    L.ref_pack_int4_codes.argtypes = [vp, vp, sz, sz, C.c_int, vp, vp]
+    L.ref_pack_mxfp4_codes.argtypes = [vp, vp, sz, sz, vp, vp]
+    L.ref_pack_nvfp4_codes.argtypes = [vp, vp, sz, sz, C.c_float, vp, vp]
+    L.ref_unpack_int4_codes.argtypes = [vp, sz, sz, vp]
+    L.ref_unpack_e2m1_codes.argtypes = [vp, sz, sz, vp]
+    return L
+
+
+@pytest.mark.parametrize("shape", [(64, 256), (7, 384), (130, 1024)])
+@pytest.mark.parametrize("fmt,group", FORMATS)
+def test_code_packers_match_reference(qg, cuda, ref, fmt, group, shape):
+    """qgemm_pack_codes / qgemm_unpack_codes equal the reference's
+    pack_*_codes / unpack_*_codes byte for byte, out-of-range INT4 codes
+    (clamped), FP4 codes with high bits set (masked), and FP16 scale edge
+    values (overflow, underflow, inf, NaN) included."""
+    import ctypes as C
+    N, K = shape
+    rng = np.random.default_rng(N * K + group)
+    L = _ref_code_fns(ref)
+    ptr = lambda a: a.ctypes.data_as(C.c_void_p)
+    nsc = N * (K // group)
+    d_ref = np.zeros(N * K // 2, np.uint8)
+    if fmt == "int4":
+        codes = rng.integers(-12, 12, N * K).astype(np.int32)
+        sc = (rng.standard_normal(nsc) * 0.05).astype(np.float32)
+        sc[:5] = [131008.0, 1e-8, np.inf, np.nan, -3e-6]
+        s_ref = np.zeros(nsc, np.uint16)
+        assert L.ref_pack_int4_codes(ptr(codes), ptr(sc), N, K, group, ptr(d_ref), ptr(s_ref)) == 0
+        fcode = qg.INT4_G128 if group == 128 else qg.INT4_G64
+        p = qg.pack_codes(fcode, torch.from_numpy(codes).cuda(), torch.from_numpy(sc).cuda(), N, K)
+        assert np.array_equal(u8(p.data), d_ref)
+        assert np.array_equal(u16(p.scales), s_ref)
+        back = qg.unpack_codes(p).cpu().numpy()
+        q_ref = np.zeros(N * K, np.int32)
+        L.ref_unpack_int4_codes(ptr(d_ref), N, K, ptr(q_ref))
+        assert np.array_equal(back, q_ref)
+        assert np.array_equal(back, np.clip(codes, -8, 7))
+        again = qg.pack_codes(fcode, torch.from_numpy(back).cuda(), torch.from_numpy(sc).cuda(), N, K)
+        assert np.array_equal(u8(again.data), d_ref)
+    else:
+        codes = rng.integers(0, 256, N * K).astype(np.uint8)
+        sb = rng.integers(0, 256, nsc).astype(np.uint8)
+        s_ref = np.zeros(nsc, np.uint8)
+        if fmt == "mxfp4":
+            assert L.ref_pack_mxfp4_codes(ptr(codes), ptr(sb), N, K, ptr(d_ref), ptr(s_ref)) == 0
+            p = qg.pack_codes(qg.MXFP4, torch.from_numpy(codes).cuda(), torch.from_numpy(sb).cuda(), N, K)
+        else:
+            assert L.ref_pack_nvfp4_codes(ptr(codes), ptr(sb), N, K, 0.37, ptr(d_ref), ptr(s_ref)) == 0
+            p = qg.pack_codes(qg.NVFP4, torch.from_numpy(codes).cuda(), torch.from_numpy(sb).cuda(), N, K,
+                              tensor_scale=0.37)
+            assert p.tensor_scale == 0.37
+        assert np.array_equal(u8(p.data), d_ref)
+        assert np.array_equal(u8(p.scales), s_ref)
+        back = qg.unpack_codes(p).cpu().numpy()
+        c_ref = np.zeros(N * K, np.uint8)
+        L.ref_unpack_e2m1_codes(ptr(d_ref), N, K, ptr(c_ref))
+        assert np.array_equal(back, c_ref)
+        assert np.array_equal(back, codes & 0xF)
