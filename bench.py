@@ -738,7 +738,15 @@ def main():
     s = torch.cuda.Stream(device=dev)
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
-        for _ in range(max(3, args.warmup)):
+        # first warm-up step call by call, each followed by a synchronise, so
+        # that a device fault names the call that raised it
+        for M, name, N, K in calls:
+            try:
+                gemm(M, name, X[(M, K)])
+                torch.cuda.synchronize()
+            except Exception as e:
+                raise SystemExit(f"warm-up call (layer {name}, M={M}) failed: {e}")
+        for _ in range(max(3, args.warmup) - 1):
             step()
     torch.cuda.current_stream().wait_stream(s)
     torch.cuda.synchronize()

@@ -218,7 +218,7 @@ qgemm_status_t qgemm_grouped_gemm_w4a16(const qgemm_weights_t* w, int32_t E, con
  * kernels, writes it into every rank's Y_full [M][N] through peer pointers
  * (y_peers[d] = rank d's Y_full as mapped in this process), adds its
  * arrival to every rank's sync block (system-scope release after the
- * stores) and waits (bounded, 2 s) until every rank's arrival for this call
+ * stores) and waits (bounded, ~2 s) until every rank's arrival for this call
  * has reached its own sync block, i.e. all slices have landed in its own
  * Y_full.  Every rank makes the same
  * sequence of calls; a rank's Y_full is written by all ranks, so reuse a

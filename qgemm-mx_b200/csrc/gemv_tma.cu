@@ -512,8 +512,7 @@ k_gemv_tma(const __grid_constant__ GtGroup<MAXE> pg, const GtArgs a) {
   if (!ok) {
     atomicExch(fault, 1u);
     if (threadIdx.x == 0) {  // give copies in flight a bounded chance to land
-      const unsigned long long t0 = gtimer();
-      while (gtimer() - t0 < 50000000ull) { }
+      fault_drain();
     }
   }
   __syncthreads();

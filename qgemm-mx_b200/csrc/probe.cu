@@ -5,7 +5,7 @@
 // gives the project's HBM denominator exists in two forms, 128-bit vector
 // loads (grid-stride, sized in multiples of the SM count) and TMA bulk copies
 // (cp.async.bulk global->shared, completion on an mbarrier, no multicast).
-// Every mbarrier wait is bounded by %globaltimer; a timeout sets a device
+// Every mbarrier wait is bounded by SM cycles; a timeout sets a device
 // flag that qgemm_probe_launch reports on the next call instead of hanging.
 #include <cublasLt.h>
 #include <cublas_v2.h>
@@ -61,21 +61,17 @@ constexpr int kBulkBytes = 16384;
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
 }
-__device__ __forceinline__ unsigned long long globaltimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
-// Wait for the phase with the given parity; false after ~limit_ns.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned long long limit_ns) {
-  const unsigned long long t0 = globaltimer();
+// Wait for the phase with the given parity; false after limit SM cycles
+// (clock64 only moves forward on an SM; the driver may step %globaltimer).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned long long limit) {
+  const unsigned long long c0 = (unsigned long long)clock64();
   for (;;) {
     uint32_t ok;
     asm volatile(
         "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
         : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
     if (ok) return true;
-    if (globaltimer() - t0 > limit_ns) return false;
+    if ((unsigned long long)clock64() - c0 > limit) return false;
   }
 }
 
@@ -102,10 +98,10 @@ __global__ void __launch_bounds__(32) k_read_bulk(const uint8_t* __restrict__ in
   for (int k = 0; k < kBulkStages && c < nchunks; ++k, c += step) issue(c, k);
   uint32_t phase[kBulkStages] = {0, 0, 0, 0, 0, 0};
   for (size_t done = first; done < nchunks; done += step) {
-    if (!mbar_wait(smem_u32(&bars[s]), phase[s], 200000000ull)) {  // 200 ms
+    if (!mbar_wait(smem_u32(&bars[s]), phase[s], 400000000ull)) {  // ~200 ms at 2 GHz
       atomicExch(&g_probe_timeout, 1u);
       // drain: give the copies still in flight a bounded chance to land
-      for (int k = 0; k < kBulkStages; ++k) (void)mbar_wait(smem_u32(&bars[k]), phase[k], 50000000ull);
+      for (int k = 0; k < kBulkStages; ++k) (void)mbar_wait(smem_u32(&bars[k]), phase[k], 100000000ull);
       return;
     }
     phase[s] ^= 1u;

@@ -2,8 +2,8 @@
 // loads, tcgen05 fences / commits / TMEM loads and stores, shared-memory
 // matrix and instruction descriptors for kind::f16.
 //
-// Every wait is bounded by %globaltimer: mbar_wait returns false and sets the
-// caller's fault flag once the phase has not completed within kWaitNs.
+// Every wait is bounded by SM cycles: mbar_wait returns false and sets the
+// caller's fault flag once the phase has not completed within kWaitCycles.
 #pragma once
 
 #include <cuda.h>
@@ -12,13 +12,23 @@
 
 namespace qg {
 
-constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s
+// Bounds of the device-side waits.  They count SM cycles (clock64, which
+// only moves forward on an SM) and polls, not %globaltimer: the driver may
+// step the global timer, and one step backwards wrapped the unsigned
+// difference and ended a healthy wait at once (intermittent "a bounded
+// barrier wait gave up" on an otherwise normal run, and a teardown whose
+// drain, timed the same way, freed TMEM under copies still in flight).
+constexpr unsigned long long kWaitCycles = 4000000000ull;  // ~2 s at 2 GHz, longer at lower clocks
+constexpr int kWaitMinPolls = 1000;                          // a poll sleeps up to ~1 ms
+constexpr unsigned long long kDrainCycles = 100000000ull;  // ~50 ms at 2 GHz
 
 __device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-__device__ __forceinline__ unsigned long long gtimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
+__device__ __forceinline__ unsigned long long sm_cycles() { return (unsigned long long)clock64(); }
+// After a wait gave up: let the CTA's copies and MMAs in flight land before
+// it frees TMEM and exits.
+__device__ __forceinline__ void fault_drain() {
+  const unsigned long long c0 = sm_cycles();
+  while (sm_cycles() - c0 < kDrainCycles) { }
 }
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
@@ -42,14 +52,16 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 // Bounded wait; false (and *fault set) when the phase never completes.
 __device__ __forceinline__ bool mbar_wait_flag(uint32_t bar, uint32_t parity, unsigned* fault) {
   if (mbar_try(bar, parity)) return true;
-  const unsigned long long t0 = gtimer();
-  while (!mbar_try(bar, parity)) {
-    if (gtimer() - t0 > kWaitNs) {
+  const unsigned long long c0 = sm_cycles();
+  int polls = 1;
+  for (;;) {
+    if (mbar_try(bar, parity)) return true;
+    if (polls < kWaitMinPolls) ++polls;  // saturates
+    else if (sm_cycles() - c0 > kWaitCycles) {
       atomicExch(fault, 1u);
       return false;
     }
   }
-  return true;
 }
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
   asm volatile(

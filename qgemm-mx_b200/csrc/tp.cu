@@ -10,7 +10,7 @@
 // exchange.  No library collective, no TMA on peer memory.
 //
 // The counts live in device memory, so the launches can be captured in a
-// CUDA graph and replayed.  The wait is bounded (2 s); on timeout the kernel
+// CUDA graph and replayed.  The wait is bounded (~2 s); on timeout the kernel
 // records it and qgemm_tp_status reports QGEMM_ERR_TIMEOUT.  Every rank must
 // make the same sequence of calls.
 //
@@ -151,7 +151,7 @@ qgemm_status_t qgemm_tp_status(int32_t* timed_out) {
     return fail(QGEMM_ERR_CUDA, "tp_status: reading a fault flag failed");
   f |= g | h | b;
   if (timed_out) *timed_out = (int32_t)f;
-  return f ? fail(QGEMM_ERR_TIMEOUT, "tp_gemm: a peer did not announce its slice within 2 s") : QGEMM_OK;
+  return f ? fail(QGEMM_ERR_TIMEOUT, "tp_gemm: a peer did not announce its slice within the bounded wait (~2 s)") : QGEMM_OK;
 }
 
 // A pointer inside a larger allocation (a caching allocator's block) is

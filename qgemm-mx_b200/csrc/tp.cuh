@@ -30,7 +30,9 @@
 namespace qg {
 
 constexpr int kTpMaxWorld = 8;
-constexpr unsigned long long kTpWaitNs = 2000000000ull;  // 2 s
+// The completion wait's bound in SM cycles (clock64 moves only forward on an
+// SM; the driver may step %globaltimer): ~2 s at 2 GHz, longer at lower clocks.
+constexpr unsigned long long kTpWaitCycles = 4000000000ull;
 constexpr uint32_t kTpCallUnits = 1u << 16;              // arrival units per call and sender
 
 struct TpOut {
@@ -48,11 +50,7 @@ __device__ __forceinline__ void tp_store(const TpOut& t, size_t m, int n, __nv_b
   for (int d = 0; d < t.world; ++d) t.y[d][off] = b;
 }
 
-__device__ __forceinline__ unsigned long long tp_gtimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
+__device__ __forceinline__ unsigned long long tp_cycles() { return (unsigned long long)clock64(); }
 
 // Called by every thread of every CTA after its last Y store; a wait that
 // gives up sets *fault (the calling kernel's own flag).
@@ -75,12 +73,12 @@ __device__ __forceinline__ void tp_finish(const TpOut& t, unsigned* fault) {
   expect = __shfl_sync(0xFFFFFFFFu, expect, 0);
   bool ok = true;
   if (tid < t.world) {
-    const unsigned long long t0 = tp_gtimer();
+    const unsigned long long c0 = tp_cycles();
     for (;;) {
       uint32_t v;
       asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine + tid) : "memory");
       if ((int32_t)(v - expect) >= 0) break;
-      if (tp_gtimer() - t0 > kTpWaitNs) { ok = false; break; }
+      if (tp_cycles() - c0 > kTpWaitCycles) { ok = false; break; }
     }
   }
   if (!ok) atomicExch(fault, 1u);

@@ -12,7 +12,7 @@
 // TMEM (TS form, below); K is split across CTAs when the tile count alone
 // does not fill the SMs, with a deterministic last-arriver reduction.
 //
-// Every mbarrier wait is bounded by %globaltimer; on timeout the kernel sets
+// Every mbarrier wait is bounded by SM cycles; on timeout the kernel sets
 // g_umma_fault, gives its in-flight copies a bounded chance to land, frees its
 // TMEM and returns (qgemm_umma_status reports it).
 #include <cuda.h>
@@ -326,8 +326,7 @@ k_umma_ts(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUt
   }
 
   if (!ok && threadIdx.x == 0) {
-    const unsigned long long t0 = gtimer();
-    while (gtimer() - t0 < 50000000ull) { }
+    fault_drain();
   }
   tc_fence_before();
   __syncthreads();

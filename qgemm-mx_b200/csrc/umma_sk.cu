@@ -548,8 +548,7 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
   if (!ok) {
     atomicExch(fault, 1u);
     if (threadIdx.x == 0) {  // give copies and MMAs in flight a bounded chance to land
-      const unsigned long long t0 = gtimer();
-      while (gtimer() - t0 < 50000000ull) { }
+      fault_drain();
     }
   }
   tc_fence_before();
