@@ -176,8 +176,10 @@ def test_tp_gemm_two_gpus_matches_oracle(O, orc):
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
     world = 2
+    # decode (TMA and LDG-fed), stream-K tcgen05, and block-scaled tcgen05 with
+    # split tiles (its fixup kernel stores the slices and runs the exchange)
     cases = [("mxfp4", 1024, 1024, 1), ("mxfp4", 2048, 4096, 8), ("nvfp4", 768, 1024, 40), ("int4", 512, 1024, 5),
-             ("mxfp4", 1024, 512, 70)]
+             ("mxfp4", 1024, 512, 70), ("mxfp4", 2048, 8192, 32)]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
