@@ -198,10 +198,10 @@ qgemm_status_t qgemm_gemm_w4a16_f32(const qgemm_weights_t* w, const uint16_t* X,
  * grouped / MoE variant with variable M per expert
  * (docs/PROJECT-v2.0-fp4-hopper.md:89-90, MASTER_EXECUTION_PLAN.md:249) and
  * does not build it; each expert's result is a qgemm_gemm_w4a16 result
- * (same bounds against ref_gemm.hpp:15-27).  MXFP4 / NVFP4 experts with
- * 1 <= M[e] <= 16 run up to 32 at a time as one X-preparation launch and one
- * decode-GEMM launch whose stream-K iteration space covers all of them;
- * other experts run as qgemm_gemm_w4a16 calls on the same stream.
+ * (same bounds against ref_gemm.hpp:15-27).  Experts with 1 <= M[e] <= 16
+ * (any format, K % 256 == 0) run up to 32 at a time as one X-preparation
+ * launch and one decode-GEMM launch whose stream-K iteration space covers all
+ * of them; other experts run as qgemm_gemm_w4a16 calls on the same stream.
  * workspace: qgemm_grouped_workspace_size(w, E, max_m) bytes serve every call
  * whose M[e] <= max_m; zero it once (qgemm_workspace_init).  A workspace
  * sized for both also serves qgemm_gemm_w4a16 calls. */

@@ -80,7 +80,9 @@ struct GtCfg {
   static constexpr int CONS = WPG * UG;
   static constexpr int THREADS = 32 * (kGtProd + CONS);
   static constexpr int MPAD = 8 * NT;
-  static constexpr int SB = (FMT == 0) ? kGtUnitK / 32 : kGtUnitK / 16;   // scale bytes per row per unit
+  // scale bytes per row per unit: E8M0 / 32, E4M3 / 16, FP16 / 128, FP16 / 64
+  static constexpr int SB = FMT == 0 ? kGtUnitK / 32 : FMT == 1 ? kGtUnitK / 16 : FMT == 2 ? 2 * kGtUnitK / 128
+                                                                                           : 2 * kGtUnitK / 64;
   static constexpr int W_BYTES = kGtRows * kGtUnitK / 2;                // 16 KB
   static constexpr int X_BYTES = MPAD * kGtUnitK * 2;
   static constexpr int XF_BYTES = 128;                                  // MPAD row factors 2^s (float)
@@ -174,13 +176,20 @@ __global__ void __launch_bounds__(kXuWarps * 32) k_xprep_units(const __grid_cons
       sc = sc < -126 ? -126 : (sc > 114 ? 114 : sc);
     }
     const float inv = u2f((uint32_t)(127 - sc) << 23);  // 2^-s
+    float xv[8];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      xv[2 * q] = u2f(w4[q] << 16) * inv;
+      xv[2 * q + 1] = u2f(w4[q] & 0xFFFF0000u) * inv;
+    }
     __half2 o[4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) o[q] = __floats2half2_rn(u2f(w4[q] << 16) * inv, u2f(w4[q] & 0xFFFF0000u) * inv);
+    for (int q = 0; q < 4; ++q)  // INT4: pairs (q, q + 4), the order int4x8_to_f16 widens codes in
+      o[q] = fmt == 2 ? __floats2half2_rn(xv[q], xv[q + 4]) : __floats2half2_rn(xv[2 * q], xv[2 * q + 1]);
     o4 = *reinterpret_cast<const uint4*>(o);
     f = u2f((uint32_t)(127 + sc) << 23);  // 2^s
   }
-  *reinterpret_cast<uint4*>(unit + m * (kGtUnitK * 2) + xg_pos(fmt, lane, m) * 16) = o4;
+  *reinterpret_cast<uint4*>(unit + m * (kGtUnitK * 2) + xg_pos(fmt == 0 ? 0 : 1, lane, m) * 16) = o4;
   if (lane == 0) reinterpret_cast<float*>(unit + mpad * (kGtUnitK * 2))[m] = f;
 }
 
@@ -211,10 +220,17 @@ __device__ __forceinline__ void gt_unit_pass(float (&accu)[RPW][NT][4], const ui
           for (int b = 0; b < 4; ++b)
             cw[r][h][b] = *reinterpret_cast<const uint32_t*>(wr + ((((uint32_t)(4 * c + b)) ^ sw) << 4) + 4 * j);
           cs[r][h] = *reinterpret_cast<const uint32_t*>(SC + row * SB + 4 * c);
-        } else {         // 16 contiguous bytes
+        } else if (FMT == 3) {  // INT4 g64: 8 bytes of each 64-group, both groups' FP16 scales
+          const uint2 lo = *reinterpret_cast<const uint2*>(wr + ((((uint32_t)(4 * c + (j >> 1))) ^ sw) << 4) + 8 * (j & 1));
+          const uint2 hi =
+              *reinterpret_cast<const uint2*>(wr + ((((uint32_t)(4 * c + 2 + (j >> 1))) ^ sw) << 4) + 8 * (j & 1));
+          cw[r][h][0] = lo.x; cw[r][h][1] = lo.y; cw[r][h][2] = hi.x; cw[r][h][3] = hi.y;
+          cs[r][h] = *reinterpret_cast<const uint32_t*>(SC + row * SB + 4 * c);
+        } else {         // NVFP4 / INT4 g128: 16 contiguous bytes
           const uint4 v = *reinterpret_cast<const uint4*>(wr + ((((uint32_t)(4 * c + j)) ^ sw) << 4));
           cw[r][h][0] = v.x; cw[r][h][1] = v.y; cw[r][h][2] = v.z; cw[r][h][3] = v.w;
-          cs[r][h] = *reinterpret_cast<const uint16_t*>(SC + row * SB + 8 * c + 2 * j);
+          if (FMT == 1) cs[r][h] = *reinterpret_cast<const uint16_t*>(SC + row * SB + 8 * c + 2 * j);
+          else cs[r][h] = *reinterpret_cast<const uint16_t*>(SC + row * SB + 2 * c);  // INT4 g128: the chunk's FP16 scale
         }
       }
 #pragma unroll
@@ -223,8 +239,10 @@ __device__ __forceinline__ void gt_unit_pass(float (&accu)[RPW][NT][4], const ui
       const uint8_t* xr = X + m * (kGtUnitK * 2);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const int idx = (FMT == 0) ? 16 * c + 4 * q + j : 16 * c + 4 * j + q;  // 8-f16 chunk of the unit
-        const uint4 v = *reinterpret_cast<const uint4*>(xr + xg_pos(FMT, idx, m) * 16);
+        // 8-f16 chunk of the unit this lane's q-th X word quad comes from
+        const int idx = FMT == 0 ? 16 * c + 4 * q + j
+                                 : FMT == 3 ? 16 * c + 8 * (q >> 1) + 2 * j + (q & 1) : 16 * c + 4 * j + q;
+        const uint4 v = *reinterpret_cast<const uint4*>(xr + xg_pos(FMT == 0 ? 0 : 1, idx, m) * 16);
         cx[t][4 * q] = v.x; cx[t][4 * q + 1] = v.y; cx[t][4 * q + 2] = v.z; cx[t][4 * q + 3] = v.w;
       }
     }
@@ -310,8 +328,9 @@ k_gemv_tma(const __grid_constant__ GtGroup<MAXE> pg, const GtArgs a) {
         n = n < a.N ? n : a.N - 1;  // rows past N: TMA zero-fills their codes
         const uint8_t* src = pg.scales[prob(p_tile)] + (size_t)n * srow + (size_t)p_ks * C::SB;
         const uint32_t dst = base + (uint32_t)(S_off(s) + row * C::SB);
-        if (FMT == 0) asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
-        else asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+        if (C::SB == 16) asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+        else if (C::SB == 8) asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+        else asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
       }
       asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(full_bar(s)) : "memory");
     };
@@ -526,14 +545,20 @@ k_gemv_tma(const __grid_constant__ GtGroup<MAXE> pg, const GtArgs a) {
 bool make_tma_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr, uint64_t inner, uint64_t outer,
                      uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw);
 
-// Each weight row's scales of a unit are copied as one 8-byte (MXFP4) or
-// 16-byte (NVFP4) piece: the scale array must start on such a boundary (the
-// row pitch K / 32 or K / 16 is a multiple of it since K % 256 == 0).
+// Each weight row's scales of a unit are copied as one piece of 8 (MXFP4),
+// 16 (NVFP4), 4 (INT4 g128) or 8 (INT4 g64) bytes: the scale array must start
+// on such a boundary (the row pitch is a multiple of it since K % 256 == 0).
 bool gemv_tma_supported(const qgemm_weights_t* w, int mb) {
-  const uintptr_t salign = w->format == QGEMM_FMT_MXFP4 ? 7u : 15u;
-  return mb >= 1 && mb <= 16 && (w->format == QGEMM_FMT_MXFP4 || w->format == QGEMM_FMT_NVFP4) &&
-         w->K % kGtUnitK == 0 && w->K <= (size_t)INT32_MAX / 2 && w->N <= (size_t)INT32_MAX / 2 &&
-         (reinterpret_cast<uintptr_t>(w->scales) & salign) == 0;
+  uintptr_t salign = 0;
+  switch (w->format) {
+    case QGEMM_FMT_MXFP4: salign = 7u; break;
+    case QGEMM_FMT_NVFP4: salign = 15u; break;
+    case QGEMM_FMT_INT4_G128: salign = 3u; break;
+    case QGEMM_FMT_INT4_G64: salign = 7u; break;
+    default: return false;
+  }
+  return mb >= 1 && mb <= 16 && w->K % kGtUnitK == 0 && w->K <= (size_t)INT32_MAX / 2 &&
+         w->N <= (size_t)INT32_MAX / 2 && (reinterpret_cast<uintptr_t>(w->scales) & salign) == 0;
 }
 
 struct GtPlan {
@@ -622,9 +647,16 @@ static cudaError_t launch_gt_f(bool f32, const GtGroup<MAXE>& g, const GtArgs& a
 }
 template <int MAXE, bool FAST>
 static cudaError_t launch_gt_l(int fmt, int nt, bool f32, const GtGroup<MAXE>& g, const GtArgs& a, cudaStream_t s) {
-  if (fmt == QGEMM_FMT_MXFP4)
-    return nt == 1 ? launch_gt_f<0, 1, MAXE, FAST>(f32, g, a, s) : launch_gt_f<0, 2, MAXE, FAST>(f32, g, a, s);
-  return nt == 1 ? launch_gt_f<1, 1, MAXE, FAST>(f32, g, a, s) : launch_gt_f<1, 2, MAXE, FAST>(f32, g, a, s);
+  switch (fmt) {
+    case QGEMM_FMT_MXFP4:
+      return nt == 1 ? launch_gt_f<0, 1, MAXE, FAST>(f32, g, a, s) : launch_gt_f<0, 2, MAXE, FAST>(f32, g, a, s);
+    case QGEMM_FMT_NVFP4:
+      return nt == 1 ? launch_gt_f<1, 1, MAXE, FAST>(f32, g, a, s) : launch_gt_f<1, 2, MAXE, FAST>(f32, g, a, s);
+    case QGEMM_FMT_INT4_G128:  // FP16 group scales: no fast / checked distinction
+      return nt == 1 ? launch_gt_f<2, 1, MAXE, false>(f32, g, a, s) : launch_gt_f<2, 2, MAXE, false>(f32, g, a, s);
+    default:
+      return nt == 1 ? launch_gt_f<3, 1, MAXE, false>(f32, g, a, s) : launch_gt_f<3, 2, MAXE, false>(f32, g, a, s);
+  }
 }
 // fast: every problem of the launch is in the scale-checked layout
 template <int MAXE>
@@ -645,7 +677,9 @@ static cudaError_t launch_xprep_units(const XuGroup<MAXE>& xu, int n_exp, const 
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k_xprep_units<MAXE>, xu, K, p.mpad, fmt == QGEMM_FMT_MXFP4 ? 0 : 1);
+  // X image order: 0 MXFP4, 1 NVFP4, 2 INT4 (pair permutation)
+  const int xf = fmt == QGEMM_FMT_MXFP4 ? 0 : fmt == QGEMM_FMT_NVFP4 ? 1 : 2;
+  return cudaLaunchKernelEx(&cfg, k_xprep_units<MAXE>, xu, K, p.mpad, xf);
 }
 
 static bool gt_map(CUtensorMap* m, const qgemm_weights_t* w) {

@@ -144,3 +144,50 @@ def test_layout_sizes_and_checks(qg):
     assert lib.qgemm_repack(C.byref(w), qg.SCALE_CHECKED, fake, fake, null) == qg.ERR_INVALID_ARG  # not canonical
     assert lib.qgemm_unpack(C.byref(qg._Weights(qg.INT4_G64, 1, 8, 64, 1 << 20, 1 << 21, 1.0)), fake, fake,
                             null) == qg.ERR_INVALID_ARG
+
+
+def test_launch_count_mirrors_dispatch(qg):
+    """qgemm_launch_count is host-only: which kernel a call uses and how many
+    launches it makes (MXFP4 with 9 <= M <= 128, K % 128 == 0 and a 32-byte
+    aligned code array: k_xprep_bs + k_umma_bs, plus k_bs_fixup when the
+    device's stream-K ranges split tiles, which needs its SM count: 2 without
+    a device; an X-preparation kernel + one GEMM kernel per 16-row block on
+    the decode paths; k_xprep + one tcgen05 kernel for M >= 32)."""
+    lib = qg.lib()
+    kern = qg._i32(0)
+
+    def count(fmt, N, K, M, scales=0x1000, data=0x2000):
+        w = qg._Weights(fmt, 0, N, K, C.c_void_p(data), C.c_void_p(scales), 1.0)
+        n = lib.qgemm_launch_count(C.byref(w), M, C.byref(kern))
+        return n, qg.KERNEL_NAMES.get(kern.value)
+
+    assert count(qg.MXFP4, 8192, 8192, 1) == (2, "k_gemv_tma")
+    assert count(qg.MXFP4, 8192, 8192, 8) == (2, "k_gemv_tma")
+    assert count(qg.MXFP4, 8192, 8192, 9) == (2, "k_umma_bs")
+    assert count(qg.MXFP4, 8192, 8192, 20) == (2, "k_umma_bs")
+    assert count(qg.MXFP4, 8192, 8192, 128) == (2, "k_umma_bs")
+    assert count(qg.MXFP4, 8192, 4224, 64) == (2, "k_umma_bs")      # K % 128 == 0
+    assert count(qg.MXFP4, 8192, 8192, 129) == (2, "k_umma_ts")
+    assert count(qg.MXFP4, 8192, 8192, 20, data=0x2010) == (4, "k_gemv_tma")  # codes not 32-byte aligned
+    assert count(qg.NVFP4, 8192, 8192, 16) == (2, "k_gemv_tma")
+    assert count(qg.NVFP4, 8192, 8192, 20) == (4, "k_gemv_tma")
+    assert count(qg.NVFP4, 8192, 8192, 32) == (2, "k_umma_sk")
+    assert count(qg.NVFP4, 8192, 8192, 127) == (2, "k_umma_sk")
+    assert count(qg.NVFP4, 8192, 8192, 128) == (2, "k_umma_ts")
+    assert count(qg.MXFP4, 8192, 4160, 64) == (2, "k_umma_ts")      # K % 128 != 0
+    assert count(qg.MXFP4, 8192, 4160, 1) == (2, "k_gemv")          # decode, LDG-fed
+    assert count(qg.NVFP4, 8192, 8192, 1, scales=0x1002) == (2, "k_gemv")  # scales not 4-byte aligned
+    assert count(qg.INT4_G128, 8192, 8192, 1) == (2, "k_gemv_tma")
+    assert count(qg.INT4_G64, 8192, 8192, 64) == (8, "k_gemv_tma")           # 4 blocks of 16 rows
+    assert count(qg.INT4_G128, 8192, 8064, 1) == (2, "k_gemv")              # K % 256 != 0: LDG-fed
+    assert count(qg.INT4_G64, 8192, 8192, 1, scales=0x1004) == (2, "k_gemv")  # scales not 8-byte aligned
+    w = qg._Weights(qg.MXFP4, 0, 64, 256, None, None, 1.0)
+    assert lib.qgemm_launch_count(C.byref(w), 0, C.byref(kern)) == -1
+    # K only needs each format's own divisibility; the rest is refused as the GEMM refuses it
+    assert count(qg.MXFP4, 2880, 2880, 1) == (2, "k_gemv")          # gpt_oss 2880: K % 128 = 64
+    assert count(qg.MXFP4, 2880, 2880, 33) == (2, "k_umma_ts")
+    assert count(qg.NVFP4, 200, 48, 1) == (2, "k_gemv")             # K % 32 = 16
+    assert count(qg.INT4_G64, 2880, 2880, 20) == (4, "k_gemv")
+    assert count(qg.INT4_G128, 2880, 2880, 1)[0] == -1              # 2880 % 128 != 0
+    assert count(qg.MXFP4, 64, 48, 1)[0] == -1                      # not whole 32-blocks
+    assert count(qg.NVFP4, 64, 40, 1)[0] == -1

@@ -27,7 +27,7 @@ CASES = [  # format, N, K, M, checked weight rows
     ("mxfp4", 57344, 8192, 64, 128),     # gate-up, block-scaled tcgen05 + fixup
     ("mxfp4", 8192, 28672, 32, 128),     # down, block-scaled tcgen05
     ("nvfp4", 14336, 4096, 16, 256),     # config 2, TMA decode (two n-tiles)
-    ("int4_g128", 14336, 4096, 8, 256),  # config 2 INT4, LDG decode
+    ("int4_g128", 14336, 4096, 8, 256),  # config 2 INT4, TMA decode
     ("nvfp4", 28672, 8192, 2048, 16),    # prefill, tile-per-CTA tcgen05
     ("mxfp4", 2880, 2880, 7, 256),       # unaligned K (gpt_oss_2880)
 ]

@@ -9,10 +9,12 @@ tests/gpu_util.py) and against the library's own single-expert call:
 
 * skewed routing (empty experts, 1-row experts, experts above the 16-row
   fused limit) for MXFP4, NVFP4 with a different tensor scale per expert,
-  and INT4 (every expert a regular call);
+  and INT4 g128;
 * more than 32 active experts (two fused launches);
 * one active expert: the fused launch plans exactly like the single call, so
-  the bits must match; INT4 experts run the single-call kernels: bits match;
+  the bits must match; experts above 16 rows run the single-call kernels:
+  bits match; fused INT4 experts agree with their single calls within the
+  contract (their stream-K split points differ);
 * rows that no expert owns keep their contents;
 * a realistic decode step: 32 experts of 4096 x 4096, top-2 routing of 64
   tokens with skew, sampled output blocks;
@@ -118,7 +120,11 @@ def test_int4_experts_match_single_calls(qg, cuda, O):
     for p, m in zip(experts, counts):
         if m:
             Ys = qg.gemm_w4a16(p, X[off:off + m])
-            assert torch.equal(Yg[off:off + m].view(torch.int16), Ys.view(torch.int16)), off
+            if m > 16:  # a regular call: the same kernels and plan
+                assert torch.equal(Yg[off:off + m].view(torch.int16), Ys.view(torch.int16)), off
+            else:       # fused with the other small expert
+                ok, ratio, rel = within_tolerance(Yg[off:off + m].float().cpu().numpy(), Ys.float().cpu().numpy())
+                assert ok, (off, ratio, rel)
         off += m
 
 
