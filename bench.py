@@ -116,9 +116,12 @@ def run_case(args):
     us = a.elapsed_time(b) * 1e3 / args.steps
     nb = qg.total_bytes(fcode, M, N, K)
     f = C.c_int32(0)
-    qg.lib().qgemm_umma_status(C.byref(f))  # nonzero: a bounded wait gave up (times and outputs invalid)
-    print(json.dumps({"case": args.case, "us_per_call": round(us, 3), "gbs": round(nb / us / 1e3, 1),
-                      "wait_timed_out": bool(f.value)}))
+    st = qg.lib().qgemm_umma_status(C.byref(f))  # nonzero: a bounded wait gave up (times and outputs invalid)
+    line = {"case": args.case, "us_per_call": round(us, 3), "gbs": round(nb / us / 1e3, 1),
+            "wait_timed_out": bool(f.value)}
+    if st != qg.OK:
+        line["status"] = qg.lib().qgemm_last_error_message().decode()
+    print(json.dumps(line))
 
 
 # Mixture-of-experts decode steps (expert gate-up projections, MXFP4):

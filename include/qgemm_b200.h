@@ -256,7 +256,9 @@ qgemm_status_t qgemm_gemm_w4a16_noalloc(const qgemm_weights_t* w, const uint16_t
                                         int32_t M, uint16_t* Y, void* stream);
 
 /* Synchronous: reports (and returns QGEMM_ERR_TIMEOUT) if a bounded barrier
- * wait inside the tcgen05 GEMM kernel gave up on this device.  Not capturable. */
+ * wait inside a GEMM kernel gave up on this device; *faulted is then nonzero
+ * and qgemm_last_error_message() names, per kernel family, where the first
+ * wait gave up (warp, CTA and barrier index).  Not capturable. */
 qgemm_status_t qgemm_umma_status(int32_t* faulted);
 
 /* Synchronous: waits for the device, then resets every fault flag of the

@@ -1,4 +1,4 @@
-// gemv_tma.cu -- TMA-fed decode GEMM for M <= 16 (MXFP4 / NVFP4, K % 256 == 0).
+// gemv_tma.cu -- TMA-fed decode GEMM for M <= 16 (MXFP4, NVFP4, INT4; K % 256 == 0).
 //
 // Same arithmetic as k_gemv (gemv.cu, through chunk_mma in gemv_core.cuh):
 // swap-AB mma.sync m16n8k16 with f16 operands and FP32 accumulation, exact
@@ -31,8 +31,9 @@
 //                mbarrier and issues the packed-W box (TMA, 128 rows x 128 B,
 //                128-byte swizzle) and the unit's X image with its row
 //                factors (one bulk copy); all 32 lanes copy the unit's scale
-//                bytes, one 8-byte (MXFP4) or 16-byte (NVFP4) cp.async per
-//                weight row, and arrive on the same mbarrier when they land.
+//                bytes, one 8-byte (MXFP4, INT4 g64), 16-byte (NVFP4) or
+//                4-byte (INT4 g128) cp.async per weight row, and arrive on
+//                the same mbarrier when they land.
 //                Weights and scales do not depend on the preparation grid, so
 //                the first stages' weights go out before the
 //                programmatic-launch wait.  No multicast.
@@ -295,7 +296,8 @@ k_gemv_tma(const __grid_constant__ GtGroup<MAXE> pg, const GtArgs a) {
   if (warp < kGtProd) {
     // ------------------------------ producers ---------------------------------
     const int p = warp;
-    const size_t srow = (size_t)a.K / (FMT == 0 ? 32 : 16);
+    // scale bytes per weight row: E8M0 per 32 k, E4M3 per 16 k, FP16 per 128 / 64 k
+    const size_t srow = (size_t)a.K / (FMT == 0 ? 32 : FMT == 1 ? 16 : FMT == 2 ? 64 : 32);
     // (tile, k-unit) of this producer's next unit, advanced by kGtProd units
     // per issue: no 64-bit division in the loop.
     int p_tile = (int)((it0 + p) / KS), p_ks = (int)((it0 + p) % KS);
@@ -359,6 +361,8 @@ k_gemv_tma(const __grid_constant__ GtGroup<MAXE> pg, const GtArgs a) {
   } else {
     // ------------------------------ consumers ---------------------------------
     constexpr int WPG = C::WPG;
+    static_assert(S % UG == 0 || (UG * kGtProd / (UG % kGtProd == 0 ? kGtProd : 1)) < S,
+                  "stage-release argument below: lcm(UG, producers) < S");
     const int cons = warp - kGtProd;
     const int ug = cons / WPG;                      // unit group: the units i with i % UG == ug
     const int wq = cons % WPG;                      // weight rows [16 RPW wq, 16 RPW (wq + 1)) of a unit
@@ -472,6 +476,15 @@ k_gemv_tma(const __grid_constant__ GtGroup<MAXE> pg, const GtArgs a) {
       const int len = (KS - ks0) < (niter - ib) ? (KS - ks0) : (niter - ib);
       for (int i = ib + (ug - ib % UG + UG) % UG; i < ib + len; i += UG) {
         const int s = i % S;
+        // With S % UG != 0 a stage's consecutive uses go to different groups,
+        // so this group may reach use u = i / S of stage s while use u - 1
+        // (another group's unit) has not landed; a parity wait would then take
+        // the pending phase u - 1 for the completed phase u - 2 and read the
+        // stage early.  So wait first for the release of use u - 1.  Both
+        // waits are unambiguous: this group has consumed unit i - L (L =
+        // lcm(UG, producers) < S, same producer as unit i), so that producer
+        // had issued unit i - S, which needed use u - 2 released.
+        if (S % UG != 0 && ok && i >= S) ok = mbar_wait_flag(empty_bar(s), ((i / S) + 1) & 1, fault);
         if (ok) ok = mbar_wait_flag(full_bar(s), (i / S) & 1, fault);
         ok = __all_sync(0xFFFFFFFFu, ok);
         if (ok) {
@@ -529,7 +542,7 @@ k_gemv_tma(const __grid_constant__ GtGroup<MAXE> pg, const GtArgs a) {
   }
 
   if (!ok) {
-    atomicExch(fault, 1u);
+    atomicCAS(fault, 0u, 1u);  // keeps the first site
     if (threadIdx.x == 0) {  // give copies in flight a bounded chance to land
       fault_drain();
     }
@@ -585,7 +598,7 @@ static GtPlan gt_plan(const qgemm_weights_t* w, int mb, int sm_count, int n_exp 
   if (p.T < 24LL * sm_count) {
     for (int u = 8; u <= 16; u *= 2) {
       if (p.T / u <= sm_count) {
-        p.G = (int)(p.T / u);
+        p.G = p.T / u > 0 ? (int)(p.T / u) : 1;  // fewer than u units: one CTA
         break;
       }
     }

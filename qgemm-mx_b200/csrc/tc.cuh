@@ -49,7 +49,15 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
       : "=r"(ok) : "r"(bar), "r"(parity), "r"(1000000u) : "memory");
   return ok != 0;
 }
-// Bounded wait; false (and *fault set) when the phase never completes.
+// Where a wait gave up, as the first value a fault flag takes: bit 31 set,
+// warp in bits 24..30, CTA in bits 8..23, and the barrier's index in its
+// 1024-byte-aligned barrier block (the kernels keep their mbarriers at the
+// start of such a block) in bits 0..7.
+__device__ __forceinline__ unsigned fault_site(uint32_t bar) {
+  return 0x80000000u | (((threadIdx.x >> 5) & 0x7Fu) << 24) | ((blockIdx.x & 0xFFFFu) << 8) | ((bar & 0x3FFu) >> 3);
+}
+// Bounded wait; false (and *fault set to the wait's site unless already
+// set) when the phase never completes.
 __device__ __forceinline__ bool mbar_wait_flag(uint32_t bar, uint32_t parity, unsigned* fault) {
   if (mbar_try(bar, parity)) return true;
   const unsigned long long c0 = sm_cycles();
@@ -58,7 +66,7 @@ __device__ __forceinline__ bool mbar_wait_flag(uint32_t bar, uint32_t parity, un
     if (mbar_try(bar, parity)) return true;
     if (polls < kWaitMinPolls) ++polls;  // saturates
     else if (sm_cycles() - c0 > kWaitCycles) {
-      atomicExch(fault, 1u);
+      atomicCAS(fault, 0u, fault_site(bar));
       return false;
     }
   }

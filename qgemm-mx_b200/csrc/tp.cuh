@@ -81,7 +81,7 @@ __device__ __forceinline__ void tp_finish(const TpOut& t, unsigned* fault) {
       if (tp_cycles() - c0 > kTpWaitCycles) { ok = false; break; }
     }
   }
-  if (!ok) atomicExch(fault, 1u);
+  if (!ok) atomicCAS(fault, 0u, 1u);
 }
 
 }  // namespace qg

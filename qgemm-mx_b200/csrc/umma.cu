@@ -481,9 +481,13 @@ qgemm_status_t qgemm_umma_status(int32_t* faulted) {
   const unsigned g = umma_sk_fault(), h = gemv_tma_fault(), b = umma_bs_fault();
   if (g == 0xFFFFFFFFu || h == 0xFFFFFFFFu || b == 0xFFFFFFFFu)
     return fail(QGEMM_ERR_CUDA, "umma: reading a fault flag failed");
-  f |= g | h | b;
-  if (faulted) *faulted = (int32_t)f;
-  return f ? fail(QGEMM_ERR_TIMEOUT, "umma: a bounded barrier wait gave up") : QGEMM_OK;
+  if (faulted) *faulted = (int32_t)(f | g | h | b);
+  if (!(f | g | h | b)) return QGEMM_OK;
+  // each flag holds where its kernel's first wait gave up (0x8wwcccbb: warp,
+  // CTA, barrier index) or 1
+  return fail(QGEMM_ERR_TIMEOUT,
+              "umma: a bounded barrier wait gave up (sites: tile %08x, stream-K %08x, decode %08x, block-scaled %08x)",
+              f, g, h, b);
 }
 
 qgemm_status_t qgemm_clear_faults(void) {

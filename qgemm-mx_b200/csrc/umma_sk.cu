@@ -546,7 +546,7 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
   }
 
   if (!ok) {
-    atomicExch(fault, 1u);
+    atomicCAS(fault, 0u, 1u);  // keeps the first site
     if (threadIdx.x == 0) {  // give copies and MMAs in flight a bounded chance to land
       fault_drain();
     }

@@ -49,6 +49,29 @@ def qg():
     return importlib.import_module("qgemm-mx_b200")
 
 
+@pytest.fixture(autouse=True)
+def _no_bounded_wait_gave_up(request):
+    """After every GPU test: no bounded device wait of a GEMM kernel gave up
+    during it (its outputs would be wrong even where a sampled check passed).
+    Tests that make a wait run out on purpose use other flags (tp, probe)."""
+    yield
+    if request.node.get_closest_marker("gpu") is None:
+        return
+    mod = sys.modules.get("qgemm-mx_b200")
+    if mod is None:
+        return
+    import ctypes as C
+    import torch
+    if not torch.cuda.is_available():
+        return
+    torch.cuda.synchronize()
+    f = C.c_int32(0)
+    if mod.lib().qgemm_umma_status(C.byref(f)) != mod.OK:
+        msg = mod.lib().qgemm_last_error_message().decode()
+        mod.clear_faults()
+        pytest.fail(f"a bounded device wait gave up: {msg}", pytrace=False)
+
+
 @pytest.fixture(scope="session")
 def cuda(qg):
     import torch
