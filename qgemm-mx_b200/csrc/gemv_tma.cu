@@ -96,7 +96,7 @@ struct GtCfg {
   // the others may already fill the next)
   static constexpr int PART_BYTES = 2 * (UG - 1) * kGtGroups * NT * 32 * 16;
   static constexpr int STAGES = ((200 * 1024 - PART_BYTES) / STAGE) & ~1;  // even: two producers
-  static constexpr int BYTES = 1024 + STAGES * STAGE + 2 * STAGES * 8 + 16 + PART_BYTES;
+  static constexpr int BYTES = 1024 + STAGES * STAGE + 3 * STAGES * 8 + 16 + PART_BYTES;
   static_assert(BYTES <= 232448, "shared memory");
   static_assert(STAGES >= 4, "ring depth");
 };
@@ -270,10 +270,19 @@ k_gemv_tma(const __grid_constant__ GtGroup<MAXE> pg, const GtArgs a) {
   auto XF_off = [&](int s) { return s * C::STAGE + C::W_BYTES + C::X_BYTES; };
   auto S_off = [&](int s) { return s * C::STAGE + C::W_BYTES + C::X_BYTES + C::XF_BYTES; };
   uint64_t* bars = reinterpret_cast<uint64_t*>(gbase + S * C::STAGE);
-  auto full_bar = [&](int s) { return su32(&bars[s]); };
-  auto empty_bar = [&](int s) { return su32(&bars[S + s]); };
-  unsigned* s_ticket = reinterpret_cast<unsigned*>(bars + 2 * S);
-  float4* s_part = reinterpret_cast<float4*>(bars + 2 * S + 2);  // [2][UG - 1][8 row groups][NT][32]
+  // Two fill barriers per stage, taken by the parity of the use u = i / S
+  // of stage s = i % S by unit i.  With S % UG != 0 consecutive uses of a
+  // stage go to different consumer groups, so a group may wait for use u
+  // while use u - 1 (another group's) is still in flight; on one barrier its
+  // parity wait would take that pending phase for the completed one before
+  // it.  Uses u - 1 and u are on different barriers here, and use u - 2 (the
+  // previous phase of use u's barrier) is complete by then: the group has
+  // consumed unit i - lcm(UG, producers), whose producer had issued unit
+  // i - S, which needed use u - 2 released.
+  auto full_bar = [&](int s, int u) { return su32(&bars[s + S * (u & 1)]); };
+  auto empty_bar = [&](int s) { return su32(&bars[2 * S + s]); };
+  unsigned* s_ticket = reinterpret_cast<unsigned*>(bars + 3 * S);
+  float4* s_part = reinterpret_cast<float4*>(bars + 3 * S + 2);  // [2][UG - 1][8 row groups][NT][32]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long it0 = (long long)blockIdx.x * a.T / a.G;
@@ -284,7 +293,8 @@ k_gemv_tma(const __grid_constant__ GtGroup<MAXE> pg, const GtArgs a) {
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(full_bar(s), 1 + 32);   // lane 0's expect_tx arrival (W and X) + 32 cp.async arrivals (scales)
+      for (int u = 0; u < 2; ++u)
+        mbar_init(full_bar(s, u), 1 + 32);  // lane 0's expect_tx arrival (W and X) + 32 cp.async arrivals (scales)
       mbar_init(empty_bar(s), C::WPG);  // the unit's group
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -308,21 +318,22 @@ k_gemv_tma(const __grid_constant__ GtGroup<MAXE> pg, const GtArgs a) {
     // problem of global tile gt and its tile within the problem
     auto prob = [&](int gt) { return MAXE == 1 ? 0 : gt / a.tiles; };
     auto ltile = [&](int gt) { return MAXE == 1 ? gt : gt - (gt / a.tiles) * a.tiles; };
-    auto issue_w = [&](int s) {  // lane 0: the unit's packed-W box; its X follows on the same barrier
-      mbar_expect_tx(full_bar(s), (uint32_t)(C::W_BYTES + C::X_BYTES + C::XF_BYTES));
+    // fb: the fill barrier of the unit's use of stage s
+    auto issue_w = [&](int s, uint32_t fb) {  // lane 0: the unit's packed-W box; its X follows on the same barrier
+      mbar_expect_tx(fb, (uint32_t)(C::W_BYTES + C::X_BYTES + C::XF_BYTES));
       tma_load_2d(base + (uint32_t)W_off(s), &pg.map_w[prob(p_tile)], p_ks * (kGtUnitK / 2), ltile(p_tile) * kGtRows,
-                  full_bar(s));
+                  fb);
     };
-    auto issue_x = [&](int s, int gt, int ks) {  // lane 0: the unit's f16 X image and row factors (k_xprep_units)
+    auto issue_x = [&](int s, uint32_t fb, int gt, int ks) {  // lane 0: the unit's f16 X image and row factors
       const uint8_t* src = pg.xg[prob(gt)] + (size_t)ks * (C::X_BYTES + C::XF_BYTES);
       asm volatile(
           "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-          ::"r"(base + (uint32_t)X_off(s)), "l"(src), "r"((uint32_t)(C::X_BYTES + C::XF_BYTES)), "r"(full_bar(s))
+          ::"r"(base + (uint32_t)X_off(s)), "l"(src), "r"((uint32_t)(C::X_BYTES + C::XF_BYTES)), "r"(fb)
           : "memory");
     };
     // all lanes: the unit's scale bytes, one 8-byte (MXFP4) or 16-byte (NVFP4)
     // copy per weight row, rows lane + 32 q
-    auto issue_scales = [&](int s) {
+    auto issue_scales = [&](int s, uint32_t fb) {
 #pragma unroll
       for (int q = 0; q < kGtRows / 32; ++q) {
         const int row = lane + 32 * q;
@@ -334,35 +345,36 @@ k_gemv_tma(const __grid_constant__ GtGroup<MAXE> pg, const GtArgs a) {
         else if (C::SB == 8) asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
         else asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
       }
-      asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(full_bar(s)) : "memory");
+      asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(fb) : "memory");
     };
     if (lane == 0 && MAXE == 1)
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&pg.map_w[0])) : "memory");
     const int pre = niter < S ? niter : S;
     // Weights and scales do not depend on the previous grid: the first stages'
     // go out before the programmatic-launch wait; X follows it.
-    for (int i = p; i < pre; i += kGtProd) {
-      if (lane == 0) issue_w(i % S);
-      issue_scales(i % S);
+    for (int i = p; i < pre; i += kGtProd) {  // first uses (u = 0)
+      if (lane == 0) issue_w(i, full_bar(i, 0));
+      issue_scales(i, full_bar(i, 0));
       advance();
     }
     asm volatile("griddepcontrol.wait;" ::: "memory");  // the X image is the preparation grid's output
     if (lane == 0)
-      for (int i = p; i < pre; i += kGtProd) issue_x(i % S, (int)((it0 + i) / KS), (int)((it0 + i) % KS));
+      for (int i = p; i < pre; i += kGtProd) issue_x(i, full_bar(i, 0), (int)((it0 + i) / KS), (int)((it0 + i) % KS));
     for (int i = pre + ((p - pre % kGtProd + kGtProd) % kGtProd); i < niter; i += kGtProd) {
       const int s = i % S;
+      const uint32_t fb = full_bar(s, i / S);
       if (lane == 0) ok = mbar_wait_flag(empty_bar(s), ((i / S) + 1) & 1, fault);
       ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
       if (!ok) break;
-      if (lane == 0) { issue_w(s); issue_x(s, p_tile, p_ks); }
-      issue_scales(s);
+      if (lane == 0) { issue_w(s, fb); issue_x(s, fb, p_tile, p_ks); }
+      issue_scales(s, fb);
       advance();
     }
   } else {
     // ------------------------------ consumers ---------------------------------
     constexpr int WPG = C::WPG;
     static_assert(S % UG == 0 || (UG * kGtProd / (UG % kGtProd == 0 ? kGtProd : 1)) < S,
-                  "stage-release argument below: lcm(UG, producers) < S");
+                  "fill-barrier argument: lcm(UG, producers) < S");
     const int cons = warp - kGtProd;
     const int ug = cons / WPG;                      // unit group: the units i with i % UG == ug
     const int wq = cons % WPG;                      // weight rows [16 RPW wq, 16 RPW (wq + 1)) of a unit
@@ -476,16 +488,8 @@ k_gemv_tma(const __grid_constant__ GtGroup<MAXE> pg, const GtArgs a) {
       const int len = (KS - ks0) < (niter - ib) ? (KS - ks0) : (niter - ib);
       for (int i = ib + (ug - ib % UG + UG) % UG; i < ib + len; i += UG) {
         const int s = i % S;
-        // With S % UG != 0 a stage's consecutive uses go to different groups,
-        // so this group may reach use u = i / S of stage s while use u - 1
-        // (another group's unit) has not landed; a parity wait would then take
-        // the pending phase u - 1 for the completed phase u - 2 and read the
-        // stage early.  So wait first for the release of use u - 1.  Both
-        // waits are unambiguous: this group has consumed unit i - L (L =
-        // lcm(UG, producers) < S, same producer as unit i), so that producer
-        // had issued unit i - S, which needed use u - 2 released.
-        if (S % UG != 0 && ok && i >= S) ok = mbar_wait_flag(empty_bar(s), ((i / S) + 1) & 1, fault);
-        if (ok) ok = mbar_wait_flag(full_bar(s), (i / S) & 1, fault);
+        // use u = i / S of stage s: fill barrier u % 2, its phase u / 2
+        if (ok) ok = mbar_wait_flag(full_bar(s, i / S), ((i / S) >> 1) & 1, fault);
         ok = __all_sync(0xFFFFFFFFu, ok);
         if (ok) {
           const uint8_t* W = gbase + W_off(s);
