@@ -698,12 +698,14 @@ def main():
     # allocation shared by CUDA IPC; tp_gemm writes each slice into every
     # rank's Y_full over NVLink and waits for the other slices -------------
     Yfull, y_peers, sync_peers, tpws, opened = {}, {}, [], {}, []
+    Yfull2, y_peers2 = {}, {}  # a second Y_full set for the end-to-end run's double buffering
     if world > 1:
         offs, off = {}, 256
         for M, name, N, K in calls:
             offs[(M, name)] = off
             off += (M * N * 2 + 255) // 256 * 256
-        tpbuf = torch.zeros(off, dtype=torch.uint8, device=dev)
+        payload = off - 256  # [sync block | set 0 | set 1], one allocation, one IPC handle
+        tpbuf = torch.zeros(256 + 2 * payload, dtype=torch.uint8, device=dev)
         handles = [None] * world
         dist.all_gather_object(handles, qg.ipc_handle(tpbuf))
         bases = []
@@ -719,6 +721,8 @@ def main():
             o = offs[(M, name)]
             y_peers[(M, name)] = [b + o for b in bases]
             Yfull[(M, name)] = tpbuf[o:o + M * N * 2].view(torch.bfloat16).view(M, N)
+            y_peers2[(M, name)] = [b + o + payload for b in bases]
+            Yfull2[(M, name)] = tpbuf[o + payload:o + payload + M * N * 2].view(torch.bfloat16).view(M, N)
             tpws[(M, name)] = qg.make_tp_workspace(shards[name], M)
     torch.cuda.synchronize()
     if world > 1:
@@ -785,31 +789,21 @@ def main():
 
     # ---- e2e: same step through the C-ABI with host buffers ----------------
     # Every step copies its distinct activations host -> device (pinned), runs
-    # the 12 GEMMs and reads every Y back to pinned host memory.  One GPU: two
-    # device buffer sets, so step i + 1's inputs travel on one copy stream and
-    # each finished Y of step i on another while step i's GEMMs run; events
-    # keep a buffer set from being reused before its copies and GEMMs are done.
-    # Several GPUs (Y in peer-shared buffers): the step's copies are
-    # serialised with its GEMMs, read-backs overlapping the later GEMMs.
+    # the 12 GEMMs and reads every Y back to pinned host memory.  Two device
+    # buffer sets, so step i + 1's inputs travel on one copy stream and each
+    # finished Y of step i on another while step i's GEMMs run; events keep a
+    # buffer set from being reused before its copies and GEMMs are done.
+    # Several GPUs: the two sets of Y_full are shared by every rank, and each
+    # rank reads back its own 1/world of every result (the job reads Y once).
     Xh = {k: torch.empty(v.shape, dtype=v.dtype, pin_memory=True).copy_(v.cpu()) for k, v in X.items()}
-    Yh = {k: torch.empty(v.shape, dtype=v.dtype, pin_memory=True) for k, v in (Yfull or Y).items()}
     Xd = {(M, K): torch.empty_like(X[(M, K)]) for (M, K) in X}
     h2d = sum(v.numel() * 2 for v in Xh.values())
-    d2h = sum(M * N * 2 for M, name, N, K in calls)
-    cs = torch.cuda.Stream(device=dev)
-    done = {(M, name): torch.cuda.Event() for M, name, N, K in calls}
-
-    def e2e_step():
-        main = torch.cuda.current_stream()
-        for key in Xd:
-            Xd[key].copy_(Xh[key], non_blocking=True)
-        for M, name, N, K in calls:
-            gemm(M, name, Xd[(M, K)])
-            done[(M, name)].record(main)
-            cs.wait_event(done[(M, name)])
-            with torch.cuda.stream(cs):
-                Yh[(M, name)].copy_((Yfull or Y)[(M, name)], non_blocking=True)
-        main.wait_stream(cs)  # the step ends when every result is on the host
+    d2h = sum(M * N * 2 for M, name, N, K in calls)  # all of Y, once per step for the whole job
+    if world == 1:
+        Yh = {k: torch.empty(v.shape, dtype=v.dtype, pin_memory=True) for k, v in Y.items()}
+    else:
+        Yh = {(M, name): torch.empty(M * N // world, dtype=torch.bfloat16, pin_memory=True)
+              for M, name, N, K in calls}
 
     if world == 1:
         Xd2 = [Xd, {k: torch.empty_like(v) for k, v in Xd.items()}]
@@ -850,33 +844,75 @@ def main():
             main.wait_stream(ds)  # the run ends when every result is on the host
             main.wait_stream(hs)
     else:
+        # A rank's step i + 1 writes set (i + 1) % 2 of every rank's Y_full,
+        # and it starts only after the exchange of the last call of step i
+        # completed on every rank.  Each rank enters that last call after its
+        # own read-back of step i - 1 (the same set) finished, so no rank
+        # overwrites a set another rank is still reading.
+        Xd2 = [Xd, {k: torch.empty_like(v) for k, v in Xd.items()}]
+        Yf2, yp2 = [Yfull, Yfull2], [y_peers, y_peers2]
+        hs, ds = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+        x_ready = [torch.cuda.Event(), torch.cuda.Event()]
+        x_free = [torch.cuda.Event(), torch.cuda.Event()]
+        y_free = [torch.cuda.Event(), torch.cuda.Event()]
+        ydone = {(M, name): torch.cuda.Event() for M, name, N, K in calls}
+
+        def h2d_into(i):
+            b = i % 2
+            hs.wait_event(x_free[b])
+            with torch.cuda.stream(hs):
+                for key in Xd2[b]:
+                    Xd2[b][key].copy_(Xh[key], non_blocking=True)
+            x_ready[b].record(hs)
+
         def e2e_run(nsteps):
-            for _ in range(nsteps):
-                e2e_step()
+            main = torch.cuda.current_stream()
+            for ev in x_ready + x_free + y_free:
+                ev.record(main)
+            h2d_into(0)
+            for i in range(nsteps):
+                b = i % 2
+                if i + 1 < nsteps:
+                    h2d_into(i + 1)
+                main.wait_event(x_ready[b])
+                for ci, (M, name, N, K) in enumerate(calls):
+                    if ci == len(calls) - 1:
+                        main.wait_event(y_free[1 - b])  # this rank's read-back of step i - 1 is done
+                    qg.tp_gemm(shards[name], Xd2[b][(M, K)], world, rank, yp2[b][(M, name)], sync_peers,
+                               tpws[(M, name)])
+                    ydone[(M, name)].record(main)
+                    ds.wait_event(ydone[(M, name)])
+                    part = M * N // world
+                    with torch.cuda.stream(ds):
+                        Yh[(M, name)].copy_(Yf2[b][(M, name)].view(-1)[rank * part:(rank + 1) * part],
+                                            non_blocking=True)
+                x_free[b].record(main)
+                y_free[b].record(ds)
+            main.wait_stream(ds)  # the run ends when every result is on the host
+            main.wait_stream(hs)
 
     e2e_run(max(3, args.warmup))
     torch.cuda.synchronize()
     # the end-to-end run is captured as one graph of all its steps: bounded so
     # the capture stays small (the device-side region above runs --steps)
     e2e_steps = min(args.steps, 100)
-    g_e2e = None
-    if world == 1:
-        # the whole run (every step's copies in and out and its 12 C-ABI calls)
-        # as one CUDA graph, as the device-side number is taken: the host then
-        # does not pace the GPU; one untimed replay, then the timed one
-        g_e2e = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g_e2e):
-            e2e_run(e2e_steps)
-        g_e2e.replay()
-        torch.cuda.synchronize()
+    # the whole run (every step's copies in and out and its 12 C-ABI calls) as
+    # one CUDA graph, as the device-side number is taken: the host then does
+    # not pace the GPU; one untimed replay, then the timed one (several GPUs:
+    # the exchange inside the kernels is the only cross-rank step, no library
+    # collective is captured)
+    g_e2e = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_e2e):
+        e2e_run(e2e_steps)
+    if world > 1:
+        dist.barrier()
+    g_e2e.replay()
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    if g_e2e is not None:
-        g_e2e.replay()
-    else:
-        e2e_run(e2e_steps)
+    g_e2e.replay()
     e1.record()
     torch.cuda.synchronize()
     if world == 1:  # the read-backs of the last step equal a fresh call (the kernels are deterministic)
@@ -969,7 +1005,8 @@ def main():
                             "calls, median of 20); cublas_bf16_us: dense bf16 W of the same shape, rotated",
             **({"fp8_baseline": fp8} if fp8 else {}),
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d * world,
-                    "d2h_bytes_per_step": d2h * world, "steps": e2e_steps},
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                    "copies": "whole job per step: every rank's X in; Y out once (each rank its 1/world)"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
                          "kernel": dom, "share": round(per_kernel[dom]["us"] / sum(v["us"] for v in per_kernel.values()), 3),
@@ -989,7 +1026,7 @@ def main():
     if world > 1:
         torch.cuda.synchronize()
         qg.tp_status()
-        del graph
+        del graph, g_e2e
         dist.barrier()  # no rank unmaps while a peer may still write into it
         for b0 in opened:
             qg.ipc_close(b0)
