@@ -89,6 +89,11 @@ def test_tp_wait_gives_up_when_a_peer_never_arrives(qg, cuda, O, orc, M, kernel)
     flag = C.c_int32(0)
     st = qg.lib().qgemm_tp_status(C.byref(flag))
     assert st == qg.ERR_TIMEOUT and flag.value != 0
+    # the GEMM status names the kernel family whose flag the exchange set
+    # (1: the exchange's wait, not an mbarrier site)
+    st = qg.lib().qgemm_umma_status(C.byref(flag))
+    family = {"k_gemv_tma": "decode", "k_umma_bs": "block-scaled"}[kernel]
+    assert st == qg.ERR_TIMEOUT and f"{family} 00000001" in qg.lib().qgemm_last_error_message().decode()
     # this rank's own slice still landed in its Y_full
     Yref = orc.w4a16_gemm(fmt, d, s, N_loc, K, Xh, nthreads=16)
     Yb = O.bf16_bits_to_f32(O.f32_to_bf16_bits(Yref)).reshape(M, N_loc)
