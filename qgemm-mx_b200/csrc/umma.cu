@@ -20,6 +20,7 @@
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
+#include "gemv_core.cuh"
 #include "tc.cuh"
 
 namespace qg {
@@ -228,7 +229,14 @@ k_umma_ts(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUt
 #pragma unroll
         for (int i = 0; i < 16; ++i) o[i] = hmul2_f16x2(o[i], f);
       } else {
-        const uint32_t f0 = f16x2_e4m3(sc & 0xFFu), f1 = f16x2_e4m3((sc >> 8) & 0xFFu);
+        // normal E4M3 codes by bit placement; zero, subnormal or NaN codes
+        // anywhere in the warp through the exact decoder (one uniform branch)
+        uint32_t f0, f1;
+        const bool fast = e4m3x2_to_f16x2_fast(sc & 0xFFFFu, f0, f1);
+        if (__any_sync(0xFFFFFFFFu, !fast)) {
+          f0 = f16x2_e4m3(sc & 0xFFu);
+          f1 = f16x2_e4m3((sc >> 8) & 0xFFu);
+        }
 #pragma unroll
         for (int i = 0; i < 16; ++i) o[i] = hmul2_f16x2(o[i], i < 8 ? f0 : f1);
       }
