@@ -242,19 +242,17 @@ k_umma_ts(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUt
       }
       return true;
     };
-    // Pipeline: the TMEM store of step ks is in flight while step ks+1 is
-    // produced; then wait for the store and release step ks to the MMA.
-    uint32_t cur[16], nxt[16];
+    // Each step is released to the MMA as soon as its TMEM store has
+    // landed; the next step is widened after that.
+    uint32_t cur[16];
     if (ksteps > 0) ok = produce(0, load_scale(kbeg), cur);
     for (int ks = 0; ks < ksteps && ok; ++ks) {
       const int sa = ks % kTsAStages;
       tmem_st16(tmem_a + ((uint32_t)(32 * q) << 16) + (uint32_t)(sa * 32 + 16 * h), cur);
-      if (ks + 1 < ksteps) ok = produce(ks + 1, load_scale(kbeg + ks + 1), nxt);
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
       mbar_arrive(aready_bar(sa));
-#pragma unroll
-      for (int i = 0; i < 16; ++i) cur[i] = nxt[i];
+      if (ks + 1 < ksteps) ok = produce(ks + 1, load_scale(kbeg + ks + 1), cur);
     }
 
     // epilogue: the warps of half 0 (one per TMEM lane quadrant) drain the
