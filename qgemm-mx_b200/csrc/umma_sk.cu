@@ -344,7 +344,8 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
       for (int u = 0; u < 16; ++u) o[u] = hmul2_f16x2(o[u], u < 8 ? f_lo : f_hi);
     };
     // Software pipeline: step i's codes and scales were loaded during step
-    // i - 1; step i + 1's are loaded while step i's TMEM store is in flight.
+    // i - 1; step i + 1's are loaded once step i's TMEM store has landed and
+    // the step is released (an earlier release feeds the MMA sooner).
     int kt = (int)(it0 % KS), seg = 0, rb = 0;
     int sa = 0;                 // TMEM A stage of step i
     uint32_t afree_ph = 1u;     // parity of afree_bar(sa) to wait for (from the second round on)
@@ -399,12 +400,13 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
       ok = __all_sync(0xFFFFFFFFu, ok);
       if (!ok) break;
       tmem_st32(tmem_a + t_lane + (uint32_t)(sa * 128 + 32 * j), o);
-      int nxt_s = cur_s;
-      if (i + 1 < niter) ok = load_step(c0, c1, sc, nxt_s);  // overlaps the store
+      // release the step as soon as its store has landed, then load the next
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(aready_bar(sa));
+      int nxt_s = cur_s;
+      if (i + 1 < niter) ok = load_step(c0, c1, sc, nxt_s);
       cur_s = nxt_s;
       if (++sa == AST) { sa = 0; afree_ph ^= 1u; }
       if (++kt == KS) kt = 0;
