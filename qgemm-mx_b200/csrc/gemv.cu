@@ -652,13 +652,13 @@ qgemm_status_t gemm_gemv_tma(const qgemm_weights_t* w, const uint16_t* X, int mb
 // [counters | partials | X image] (gemv_tma.cu)
 static size_t decode_tma_workspace(const qgemm_weights_t* w, int sms) { return gemv_tma_workspace(w, sms); }
 
-// The tcgen05 paths (dequantised W in TMEM) take MXFP4 / NVFP4 with M >= 32:
+// The tcgen05 paths (dequantised W in TMEM) take M >= 32: MXFP4 / NVFP4 on
 // the persistent stream-K kernel for M < 128 and K % 256 == 0 (umma_sk.cu),
-// the tile-per-CTA kernel with K splits otherwise (K % 64 == 0, umma.cu).
-// Their workspace holds the f16 copy of X, its row factors and the split
-// tiles' tickets and partial sums.
+// every format on the tile-per-CTA kernel with K splits otherwise (K % 64 ==
+// 0, umma.cu).  Their workspace holds the f16 copy of X, its row factors and
+// the split tiles' tickets and partial sums.
 static bool use_umma(const qgemm_weights_t* w, int M) {
-  return M >= 32 && (w->format == QGEMM_FMT_MXFP4 || w->format == QGEMM_FMT_NVFP4) && w->K % 64 == 0;
+  return M >= 32 && w->K % 64 == 0;
 }
 static int sm_count_or_zero() {
   DevProps dp;
@@ -723,7 +723,9 @@ qgemm_status_t gemm_decode_ex(const qgemm_weights_t* w, const uint16_t* X, int M
       return gemm_umma_sk(w, xh, xs, M, Y, f32, tickets, part, sm_count_or_zero(), s, tp);
     }
     if (tp) return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "gemm: no tensor-parallel output on this path");
-    QG_CUDA_RET(launch_xprep(X, M, M, (int)w->K, 0, 0, 0, xh, xs, s));
+    // INT4: X in the pair order int4x8_to_f16 widens codes in
+    const int perm = (w->format == QGEMM_FMT_INT4_G128 || w->format == QGEMM_FMT_INT4_G64) ? 1 : 0;
+    QG_CUDA_RET(launch_xprep(X, M, M, (int)w->K, perm, 0, 0, xh, xs, s));
     return gemm_umma_ts(w, xh, xs, M, Y, f32, umma_split_count(w, M), tickets, part, s);
   }
   if (gemv_tma_supported(w, M < kMaxM ? M : kMaxM)) {

@@ -1,5 +1,5 @@
 // umma.cu -- tile-per-CTA tcgen05 (5th-generation tensor core) W4A16 GEMM
-// for M >= 128 (and for 32 <= M < 128 when K % 256 != 0).
+// for M >= 128 (and for 32 <= M < 128 when K % 256 != 0, and for INT4).
 //
 // Y[M,N] = X[M,K] . W[N,K]^T, W packed in the reference layouts
 // (titoatwork/qgemm-mx include/qgemm/pack.hpp:14-85); X arrives as the f16
@@ -65,6 +65,12 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
 //          t - b_n >= -23 (a 37-binade window below the row's largest block);
 //          blocks further down are flushed to zero.  The epilogue multiplies
 //          row n by 2^b_n and column m by the X prescale 2^s_m.
+//   INT4   q (exact in f16) times the FP16 group scale, rounded to f16
+//          (exact while q s needs <= 11 significant bits, e.g. scales of up
+//          to 8 bits; otherwise within 2^-11 relative); rows whose scales
+//          could overflow f16 are folded by a power of two the epilogue
+//          multiplies back.  Codes widen in (c_i, c_i+4) pairs, so X comes
+//          with k_xprep's INT4 pair permutation.
 // Warps: 0 TMA producer, 1 MMA issuer, 2..9 dequant (two per TMEM lane
 // quadrant, each covering 32 of the 64 k of a stage) and epilogue.
 
@@ -162,10 +168,11 @@ k_umma_ts(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUt
     const bool live = n < a.N;
     const uint8_t* sc8 = static_cast<const uint8_t*>(a.scales);
     // Scale bytes come 16 at a time: a group covers SPG K-steps (MXFP4: 8
-    // steps x 2 blocks, NVFP4: 4 steps x 4 blocks).  vec needs the row's
-    // scale run to start on a 16-byte boundary; otherwise one load per step.
-    constexpr int SPG = (FMT == 0) ? 8 : 4;
-    const size_t srow_bytes = (size_t)a.K / (FMT == 0 ? 32 : 16);
+    // steps x 2 blocks, NVFP4: 4 steps x 4 blocks, INT4 g128: 16 steps x 1/2
+    // group, INT4 g64: 8 steps x 1 group).  vec needs the row's scale run to
+    // start on a 16-byte boundary; otherwise one load per step.
+    constexpr int SPG = (FMT == 0) ? 8 : (FMT == 1) ? 4 : (FMT == 2) ? 16 : 8;
+    const size_t srow_bytes = (size_t)a.K / (FMT == 0 ? 32 : FMT == 1 ? 16 : FMT == 2 ? 64 : 32);
     const uint8_t* srow = sc8 + (size_t)n * srow_bytes;
     const bool vec = (srow_bytes % 16 == 0) && ((reinterpret_cast<uintptr_t>(sc8) & 15u) == 0);
     int rbase = 0;  // MXFP4: per-row base exponent
@@ -189,6 +196,27 @@ k_umma_ts(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUt
       }
       rbase = (tmax < 0) ? 0 : tmax - 127 - 13;
     }
+    // INT4: q * s is formed in f16 (exact while it needs at most 11
+    // significant bits, as for scales of up to 8 bits); rows whose largest
+    // FP16 scale field e would overflow f16 (|q s| < 2^(e - 11)) are folded
+    // by 2^-rbase, rbase = max(0, e - 26), and multiplied back in the epilogue.
+    if (FMT >= 2 && live) {
+      int emax = 0;
+      auto fold16 = [&](uint32_t v) {
+        const int e0 = (int)((v >> 10) & 0x1Fu), e1 = (int)((v >> 26) & 0x1Fu);
+        emax = max(emax, e0 == 31 ? 0 : e0);
+        emax = max(emax, e1 == 31 ? 0 : e1);
+      };
+      if (vec) {
+        for (size_t i = 0; i < srow_bytes; i += 16) {
+          const uint4 v = *reinterpret_cast<const uint4*>(srow + i);
+          fold16(v.x); fold16(v.y); fold16(v.z); fold16(v.w);
+        }
+      } else {
+        for (size_t i = 0; i < srow_bytes; i += 2) fold16(*reinterpret_cast<const uint16_t*>(srow + i));
+      }
+      rbase = emax > 26 ? emax - 26 : 0;
+    }
     uint4 grp_cur = make_uint4(0, 0, 0, 0), grp_nxt = make_uint4(0, 0, 0, 0);
     int grp_id = -1;
     auto load_group = [&](int g) -> uint4 {
@@ -200,6 +228,8 @@ k_umma_ts(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUt
       if (!live) return 0u;
       if (!vec) {
         if (FMT == 0) return srow[gk * 2 + h];
+        if (FMT == 2) return *reinterpret_cast<const uint16_t*>(srow + (gk >> 1) * 2);
+        if (FMT == 3) return *reinterpret_cast<const uint16_t*>(srow + gk * 2);
         return *reinterpret_cast<const uint16_t*>(srow + gk * 4 + 2 * h);
       }
       const int g = gk / SPG;
@@ -208,7 +238,9 @@ k_umma_ts(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUt
         grp_nxt = load_group(g + 1);
         grp_id = g;
       }
-      const int byte = (FMT == 0) ? (gk % SPG) * 2 + h : (gk % SPG) * 4 + 2 * h;
+      const int byte = (FMT == 0) ? (gk % SPG) * 2 + h
+                     : (FMT == 1) ? (gk % SPG) * 4 + 2 * h
+                     : (FMT == 2) ? ((gk % SPG) >> 1) * 2 : (gk % SPG) * 2;
       const int wi = byte >> 2;
       const uint32_t wv = wi == 0 ? grp_cur.x : wi == 1 ? grp_cur.y : wi == 2 ? grp_cur.z : grp_cur.w;
       return (FMT == 0) ? ((wv >> (8 * (byte & 3))) & 0xFFu) : ((wv >> (8 * (byte & 3))) & 0xFFFFu);
@@ -221,24 +253,40 @@ k_umma_ts(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUt
       if (ks >= kTsAStages && !mbar_wait(afree_bar(sa), ((ks / kTsAStages) + 1) & 1)) return false;
       const uint4 pk = *reinterpret_cast<const uint4*>(P_ptr(s) + r * 32 + 16 * h);  // 32 codes
       const uint32_t qw[4] = {pk.x, pk.y, pk.z, pk.w};
+      if constexpr (FMT >= 2) {
+        // INT4: pairs (c_i, c_i+4) of each 8 codes, the order the X copy of
+        // k_xprep (INT4 pair permutation) holds; times the FP16 group scale,
+        // folded by 2^-rbase
 #pragma unroll
-      for (int w4 = 0; w4 < 4; ++w4) e2m1x8_to_f16x2(qw[w4], o + 4 * w4);
-      if (FMT == 0) {
-        const uint32_t b = sc & 0xFFu;
-        const uint32_t f = (b == 0xFFu) ? 0x7E007E00u : f16x2_pow2((int)b - 127 - rbase);
+        for (int w4 = 0; w4 < 4; ++w4) {
+          uint32_t t[4];
+          int4x8_to_f16(qw[w4], t);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) o[4 * w4 + i] = t[i];
+        }
+        const uint32_t f = hmul2_f16x2((sc & 0xFFFFu) | (sc << 16), f16x2_pow2(-rbase));
 #pragma unroll
         for (int i = 0; i < 16; ++i) o[i] = hmul2_f16x2(o[i], f);
       } else {
-        // normal E4M3 codes by bit placement; zero, subnormal or NaN codes
-        // anywhere in the warp through the exact decoder (one uniform branch)
-        uint32_t f0, f1;
-        const bool fast = e4m3x2_to_f16x2_fast(sc & 0xFFFFu, f0, f1);
-        if (__any_sync(0xFFFFFFFFu, !fast)) {
-          f0 = f16x2_e4m3(sc & 0xFFu);
-          f1 = f16x2_e4m3((sc >> 8) & 0xFFu);
-        }
 #pragma unroll
-        for (int i = 0; i < 16; ++i) o[i] = hmul2_f16x2(o[i], i < 8 ? f0 : f1);
+        for (int w4 = 0; w4 < 4; ++w4) e2m1x8_to_f16x2(qw[w4], o + 4 * w4);
+        if constexpr (FMT == 0) {
+          const uint32_t b = sc & 0xFFu;
+          const uint32_t f = (b == 0xFFu) ? 0x7E007E00u : f16x2_pow2((int)b - 127 - rbase);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o[i] = hmul2_f16x2(o[i], f);
+        } else {
+          // normal E4M3 codes by bit placement; zero, subnormal or NaN codes
+          // anywhere in the warp through the exact decoder (one uniform branch)
+          uint32_t f0, f1;
+          const bool fast = e4m3x2_to_f16x2_fast(sc & 0xFFFFu, f0, f1);
+          if (__any_sync(0xFFFFFFFFu, !fast)) {
+            f0 = f16x2_e4m3(sc & 0xFFu);
+            f1 = f16x2_e4m3((sc >> 8) & 0xFFu);
+          }
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o[i] = hmul2_f16x2(o[i], i < 8 ? f0 : f1);
+        }
       }
       return true;
     };
@@ -262,7 +310,7 @@ k_umma_ts(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUt
       if (ok) ok = mbar_wait(acc_bar, 0);
       tc_fence_after();
       asm volatile("griddepcontrol.wait;" ::: "memory");  // xs written by the X-preparation grid
-      const float rowf = (FMT == 0) ? ((rbase >= -126) ? u2f((uint32_t)(127 + rbase) << 23) : ldexpf(1.0f, rbase))
+      const float rowf = (FMT != 1) ? ((rbase >= -126) ? u2f((uint32_t)(127 + rbase) << 23) : ldexpf(1.0f, rbase))
                                     : a.ts;
       auto store = [&](int m, float acc) {
         if (live && m < a.M) {
@@ -435,8 +483,9 @@ size_t umma_split_workspace(const qgemm_weights_t* w, int M, int splits) {
 
 qgemm_status_t gemm_umma_ts(const qgemm_weights_t* w, const __half* Xh, const float* xs, int M, void* Y, bool f32,
                             int splits, unsigned* tickets, void* partials, cudaStream_t s) {
-  if (w->format != QGEMM_FMT_MXFP4 && w->format != QGEMM_FMT_NVFP4)
-    return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "umma path: MXFP4 / NVFP4 only");
+  if (w->format != QGEMM_FMT_MXFP4 && w->format != QGEMM_FMT_NVFP4 && w->format != QGEMM_FMT_INT4_G128 &&
+      w->format != QGEMM_FMT_INT4_G64)
+    return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "umma path: unknown format");
   if (w->K % kUBK != 0 || w->K > (size_t)INT32_MAX || w->N > (size_t)INT32_MAX)
     return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "umma path: K must be a multiple of %d", kUBK);
   const int bn = umma_bn_for(M);
@@ -458,10 +507,20 @@ qgemm_status_t gemm_umma_ts(const qgemm_weights_t* w, const __half* Xh, const fl
     a.partials = static_cast<float*>(partials);
   }
   cudaError_t e;
-  if (w->format == QGEMM_FMT_MXFP4)
-    e = f32 ? launch_ts_bn<0, true>(bn, mw, mx, a, xs, s) : launch_ts_bn<0, false>(bn, mw, mx, a, xs, s);
-  else
-    e = f32 ? launch_ts_bn<1, true>(bn, mw, mx, a, xs, s) : launch_ts_bn<1, false>(bn, mw, mx, a, xs, s);
+  switch (w->format) {
+    case QGEMM_FMT_MXFP4:
+      e = f32 ? launch_ts_bn<0, true>(bn, mw, mx, a, xs, s) : launch_ts_bn<0, false>(bn, mw, mx, a, xs, s);
+      break;
+    case QGEMM_FMT_NVFP4:
+      e = f32 ? launch_ts_bn<1, true>(bn, mw, mx, a, xs, s) : launch_ts_bn<1, false>(bn, mw, mx, a, xs, s);
+      break;
+    case QGEMM_FMT_INT4_G128:
+      e = f32 ? launch_ts_bn<2, true>(bn, mw, mx, a, xs, s) : launch_ts_bn<2, false>(bn, mw, mx, a, xs, s);
+      break;
+    default:
+      e = f32 ? launch_ts_bn<3, true>(bn, mw, mx, a, xs, s) : launch_ts_bn<3, false>(bn, mw, mx, a, xs, s);
+      break;
+  }
   if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "umma launch: %s", cudaGetErrorString(e));
   return QGEMM_OK;
 }

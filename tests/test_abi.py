@@ -178,7 +178,9 @@ def test_launch_count_mirrors_dispatch(qg):
     assert count(qg.MXFP4, 8192, 4160, 1) == (2, "k_gemv")          # decode, LDG-fed
     assert count(qg.NVFP4, 8192, 8192, 1, scales=0x1002) == (2, "k_gemv")  # scales not 4-byte aligned
     assert count(qg.INT4_G128, 8192, 8192, 1) == (2, "k_gemv_tma")
-    assert count(qg.INT4_G64, 8192, 8192, 64) == (8, "k_gemv_tma")           # 4 blocks of 16 rows
+    assert count(qg.INT4_G64, 8192, 8192, 20) == (4, "k_gemv_tma")           # 2 blocks of 16 rows
+    assert count(qg.INT4_G64, 8192, 8192, 64) == (2, "k_umma_ts")            # M >= 32: tcgen05
+    assert count(qg.INT4_G128, 8192, 8192, 2048) == (2, "k_umma_ts")
     assert count(qg.INT4_G128, 8192, 8064, 1) == (2, "k_gemv")              # K % 256 != 0: LDG-fed
     assert count(qg.INT4_G64, 8192, 8192, 1, scales=0x1004) == (2, "k_gemv")  # scales not 8-byte aligned
     w = qg._Weights(qg.MXFP4, 0, 64, 256, None, None, 1.0)

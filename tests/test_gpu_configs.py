@@ -155,8 +155,8 @@ def test_prefill_sampled_rows(qg, cuda, O, orc, N, K):
 PROBE_FORMATS = [("mxfp4", 32), ("nvfp4", 16), ("int4", 128), ("int4", 64)]
 # M values that route to each kernel: 1 and 8 decode (TMA or LDG), 12 block-scaled
 # (MXFP4) / decode, 40 block-scaled (MXFP4) / stream-K tcgen05 (NVFP4), 130 tile
-# tcgen05 (MXFP4 and NVFP4), INT4 always a decode kernel in 16-row blocks (TMA-fed
-# when K % 256 == 0, LDG-fed otherwise).
+# tcgen05 (MXFP4 and NVFP4); INT4: the decode kernel in 16-row blocks below
+# M = 32 (TMA-fed when K % 256 == 0), the tile tcgen05 kernel from M = 32.
 PROBE_M = [1, 8, 12, 40, 130]
 
 
