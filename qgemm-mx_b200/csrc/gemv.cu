@@ -652,14 +652,17 @@ qgemm_status_t gemm_gemv_tma(const qgemm_weights_t* w, const uint16_t* X, int mb
 // [counters | partials | X image] (gemv_tma.cu)
 static size_t decode_tma_workspace(const qgemm_weights_t* w, int sms) { return gemv_tma_workspace(w, sms); }
 
-// The tcgen05 paths (dequantised W in TMEM) take M >= 32: MXFP4 / NVFP4 on
-// the persistent stream-K kernel for M < 128 and K % 256 == 0 (umma_sk.cu),
-// every format on the tile-per-CTA kernel with K splits otherwise (K % 64 ==
-// 0, umma.cu).  Their workspace holds the f16 copy of X, its row factors and
-// the split tiles' tickets and partial sums.
+// The tcgen05 paths (dequantised W in TMEM) take M >= 32, and NVFP4 / INT4
+// from M = 17 (one pass over W instead of two 16-row decode passes; X is
+// padded to 32 zero rows): MXFP4 / NVFP4 on the persistent stream-K kernel
+// for M < 128 and K % 256 == 0 (umma_sk.cu), every format on the
+// tile-per-CTA kernel with K splits otherwise (K % 64 == 0, umma.cu).  Their
+// workspace holds the f16 copy of X, its row factors and the split tiles'
+// tickets and partial sums.
 static bool use_umma(const qgemm_weights_t* w, int M) {
-  return M >= 32 && w->K % 64 == 0;
+  return (M >= 32 || (M >= 17 && w->format != QGEMM_FMT_MXFP4)) && w->K % 64 == 0;
 }
+static int umma_ts_rows(int M) { return M < 32 ? 32 : M; }  // the tile kernel's X rows
 static int sm_count_or_zero() {
   DevProps dp;
   return device_props(&dp) == QGEMM_OK ? dp.sm_count : 0;
@@ -670,7 +673,8 @@ static int umma_split_count(const qgemm_weights_t* w, int M) {
 }
 // [tickets | xs | Xh | split partials]
 static size_t umma_xh_bytes(const qgemm_weights_t* w, int M) {
-  const int rows = umma_sk_supported(w, M) ? (M + umma_sk_bn(M) - 1) / umma_sk_bn(M) * umma_sk_bn(M) : M;
+  const int rows = umma_sk_supported(w, M) ? (M + umma_sk_bn(M) - 1) / umma_sk_bn(M) * umma_sk_bn(M)
+                                           : umma_ts_rows(M);
   return pad256((size_t)rows * w->K * sizeof(__half));
 }
 static size_t umma_workspace(const qgemm_weights_t* w, int M) {
@@ -725,7 +729,7 @@ qgemm_status_t gemm_decode_ex(const qgemm_weights_t* w, const uint16_t* X, int M
     if (tp) return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "gemm: no tensor-parallel output on this path");
     // INT4: X in the pair order int4x8_to_f16 widens codes in
     const int perm = (w->format == QGEMM_FMT_INT4_G128 || w->format == QGEMM_FMT_INT4_G64) ? 1 : 0;
-    QG_CUDA_RET(launch_xprep(X, M, M, (int)w->K, perm, 0, 0, xh, xs, s));
+    QG_CUDA_RET(launch_xprep(X, M, umma_ts_rows(M), (int)w->K, perm, 0, 0, xh, xs, s));
     return gemm_umma_ts(w, xh, xs, M, Y, f32, umma_split_count(w, M), tickets, part, s);
   }
   if (gemv_tma_supported(w, M < kMaxM ? M : kMaxM)) {

@@ -1,5 +1,6 @@
 // umma.cu -- tile-per-CTA tcgen05 (5th-generation tensor core) W4A16 GEMM
-// for M >= 128 (and for 32 <= M < 128 when K % 256 != 0, and for INT4).
+// for M >= 128 (and for 32 <= M < 128 when K % 256 != 0, and for INT4 from
+// M = 17).
 //
 // Y[M,N] = X[M,K] . W[N,K]^T, W packed in the reference layouts
 // (titoatwork/qgemm-mx include/qgemm/pack.hpp:14-85); X arrives as the f16
@@ -459,7 +460,8 @@ static cudaError_t launch_ts_bn(int bn, const CUtensorMap& mw, const CUtensorMap
 
 int umma_bn_for(int M) { return M >= 256 ? 256 : M >= 128 ? 128 : M >= 64 ? 64 : 32; }
 
-// TS path: Xh / xs are the f16 copy of X and its row factors (k_xprep).
+// TS path: Xh / xs are the f16 copy of X and its row factors (k_xprep); for
+// M < 32 Xh holds 32 rows, the ones past M zero.
 // K splits for a launch: enough CTAs to fill every SM slot when the tile
 // count alone does not, each split keeping >= 8 K-steps.
 int umma_splits(const qgemm_weights_t* w, int M, int sm_count) {
@@ -492,8 +494,8 @@ qgemm_status_t gemm_umma_ts(const qgemm_weights_t* w, const __half* Xh, const fl
   CUtensorMap mw, mx;
   if (!make_tma_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->data, w->K / 2, w->N, w->K / 2, kUBK / 2, kUBM,
                    CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !make_tma_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, Xh, w->K, (uint64_t)M, w->K * 2, kUBK, (uint32_t)bn,
-                   CU_TENSOR_MAP_SWIZZLE_128B))
+      !make_tma_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, Xh, w->K, (uint64_t)(M < 32 ? 32 : M), w->K * 2, kUBK,
+                   (uint32_t)bn, CU_TENSOR_MAP_SWIZZLE_128B))
     return fail(QGEMM_ERR_CUDA, "umma path: cuTensorMapEncodeTiled failed");
   UmmaArgs a;
   a.scales = w->scales; a.Y = Y; a.M = M; a.N = (int)w->N; a.K = (int)w->K; a.ts = w->tensor_scale;

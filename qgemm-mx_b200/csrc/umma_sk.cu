@@ -572,7 +572,8 @@ bool make_tma_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr, 
 int umma_sk_bn(int M) { return M >= 64 ? 64 : 32; }
 
 bool umma_sk_supported(const qgemm_weights_t* w, int M) {
-  return M >= 32 && M < 128 && (w->format == QGEMM_FMT_MXFP4 || w->format == QGEMM_FMT_NVFP4) &&
+  return (M >= 32 || (M >= 17 && w->format == QGEMM_FMT_NVFP4)) && M < 128 &&
+         (w->format == QGEMM_FMT_MXFP4 || w->format == QGEMM_FMT_NVFP4) &&
          w->K % kSkBK == 0 && w->K <= (size_t)INT32_MAX && w->N <= (size_t)INT32_MAX &&
          (reinterpret_cast<uintptr_t>(w->scales) & 3u) == 0;
 }

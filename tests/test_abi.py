@@ -170,7 +170,7 @@ def test_launch_count_mirrors_dispatch(qg):
     assert count(qg.MXFP4, 8192, 8192, 129) == (2, "k_umma_ts")
     assert count(qg.MXFP4, 8192, 8192, 20, data=0x2010) == (4, "k_gemv_tma")  # codes not 32-byte aligned
     assert count(qg.NVFP4, 8192, 8192, 16) == (2, "k_gemv_tma")
-    assert count(qg.NVFP4, 8192, 8192, 20) == (4, "k_gemv_tma")
+    assert count(qg.NVFP4, 8192, 8192, 17) == (2, "k_umma_sk")             # one pass, X padded to 32 rows
     assert count(qg.NVFP4, 8192, 8192, 32) == (2, "k_umma_sk")
     assert count(qg.NVFP4, 8192, 8192, 127) == (2, "k_umma_sk")
     assert count(qg.NVFP4, 8192, 8192, 128) == (2, "k_umma_ts")
@@ -178,8 +178,9 @@ def test_launch_count_mirrors_dispatch(qg):
     assert count(qg.MXFP4, 8192, 4160, 1) == (2, "k_gemv")          # decode, LDG-fed
     assert count(qg.NVFP4, 8192, 8192, 1, scales=0x1002) == (2, "k_gemv")  # scales not 4-byte aligned
     assert count(qg.INT4_G128, 8192, 8192, 1) == (2, "k_gemv_tma")
-    assert count(qg.INT4_G64, 8192, 8192, 20) == (4, "k_gemv_tma")           # 2 blocks of 16 rows
-    assert count(qg.INT4_G64, 8192, 8192, 64) == (2, "k_umma_ts")            # M >= 32: tcgen05
+    assert count(qg.INT4_G64, 8192, 8192, 16) == (2, "k_gemv_tma")
+    assert count(qg.INT4_G64, 8192, 8192, 20) == (2, "k_umma_ts")            # M >= 17: tcgen05
+    assert count(qg.INT4_G64, 8192, 8192, 64) == (2, "k_umma_ts")
     assert count(qg.INT4_G128, 8192, 8192, 2048) == (2, "k_umma_ts")
     assert count(qg.INT4_G128, 8192, 8064, 1) == (2, "k_gemv")              # K % 256 != 0: LDG-fed
     assert count(qg.INT4_G64, 8192, 8192, 1, scales=0x1004) == (2, "k_gemv")  # scales not 8-byte aligned
@@ -189,7 +190,8 @@ def test_launch_count_mirrors_dispatch(qg):
     assert count(qg.MXFP4, 2880, 2880, 1) == (2, "k_gemv")          # gpt_oss 2880: K % 128 = 64
     assert count(qg.MXFP4, 2880, 2880, 33) == (2, "k_umma_ts")
     assert count(qg.NVFP4, 200, 48, 1) == (2, "k_gemv")             # K % 32 = 16
-    assert count(qg.INT4_G64, 2880, 2880, 20) == (4, "k_gemv")
+    assert count(qg.INT4_G64, 2880, 2880, 20) == (2, "k_umma_ts")          # K % 64 == 0
+    assert count(qg.INT4_G64, 2880, 2880, 16) == (2, "k_gemv")
     assert count(qg.INT4_G128, 2880, 2880, 1)[0] == -1              # 2880 % 128 != 0
     assert count(qg.MXFP4, 64, 48, 1)[0] == -1                      # not whole 32-blocks
     assert count(qg.NVFP4, 64, 40, 1)[0] == -1

@@ -36,7 +36,7 @@ def _packed(qg, O, fmt, group, N, K, seed=0):
 
 
 WS_CASES = [  # (format, group, N, K, M values): one per dispatch path, and INT4 tails
-    ("int4", 128, 14336, 4096, [17, 18, 20, 24, 40]),   # LDG decode, first block + tail block
+    ("int4", 128, 14336, 4096, [16, 17, 18, 20, 24, 40]),  # TMA decode, then the tile tcgen05 kernel
     ("int4", 64, 4096, 4096, [1, 16, 33]),
     ("mxfp4", 32, 4096, 4096, [1, 8, 16, 64]),          # TMA decode, block-scaled
     ("nvfp4", 16, 4096, 4096, [1, 16, 40, 130]),        # TMA decode, stream-K and tile tcgen05

@@ -53,9 +53,9 @@ def test_gemm_small_all_outputs(qg, cuda, O, orc, fmt, group, M):
     Yref = orc.w4a16_gemm(fmt, d, s, N, K, X, group=group, tensor_scale=ts, nthreads=8)
     ok, ratio, rel = within_tolerance(run(qg, p, X, f32=True), Yref)
     assert ok, (ratio, rel)
-    # fp32 output: only summation order differs, except INT4 from M = 32,
+    # fp32 output: only summation order differs, except INT4 from M = 17,
     # whose tcgen05 path rounds q x scale to f16 (relative 2^-11 per weight)
-    assert rel < (1e-3 if fmt == "int4" and M >= 32 else 1e-5), rel
+    assert rel < (1e-3 if fmt == "int4" and M >= 17 else 1e-5), rel
     Yb = run(qg, p, X, f32=False)
     ok, ratio, rel = within_tolerance(Yb, O.bf16_bits_to_f32(O.f32_to_bf16_bits(Yref)).reshape(M, N))
     assert ok, (ratio, rel)

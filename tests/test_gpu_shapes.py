@@ -44,7 +44,8 @@ def test_layer_shape_all_outputs(qg, cuda, O, orc, fmt, group, N, K, ms):
         Xd = to_dev_bf16(X)
         Y = qg.gemm_w4a16(p, Xd, out_f32=True).cpu().numpy()
         ok, ratio, rel = within_tolerance(Y, Yref)
-        assert ok and rel < 1e-5, (M, ratio, rel)
+        # INT4 from M = 17 runs the tcgen05 path, which rounds q x scale to f16
+        assert ok and rel < (1e-3 if fmt == "int4" and M >= 17 else 1e-5), (M, ratio, rel)
         Yb = bf16_to_np_f32(qg.gemm_w4a16(p, Xd, out_f32=False))
         ok, ratio, rel = within_tolerance(Yb, O.bf16_bits_to_f32(O.f32_to_bf16_bits(Yref)).reshape(M, N))
         assert ok, (M, ratio, rel)
@@ -58,7 +59,7 @@ def test_layer_shape_launch_choice(qg):
     lib, kern = qg.lib(), C.c_int(0)
     for fmt, K, M, name in [(qg.MXFP4, 2880, 1, "k_gemv"), (qg.MXFP4, 2880, 16, "k_gemv"),
                             (qg.MXFP4, 2880, 33, "k_umma_ts"), (qg.MXFP4, 96, 40, "k_gemv"),
-                            (qg.INT4_G64, 2880, 20, "k_gemv")]:
+                            (qg.INT4_G64, 2880, 16, "k_gemv"), (qg.INT4_G64, 2880, 20, "k_umma_ts")]:
         data = torch.empty(16, dtype=torch.uint8, device="cuda")
         w = qg._Weights(fmt, 0, 2880, K, C.c_void_p(data.data_ptr()), C.c_void_p(data.data_ptr()), 1.0)
         assert lib.qgemm_launch_count(C.byref(w), M, C.byref(kern)) > 0

@@ -59,10 +59,10 @@ def test_noalloc_matches_oracle_and_workspace_entry_point(qg, cuda, O, orc, fmt,
     Yref_b = O.bf16_bits_to_f32(O.f32_to_bf16_bits(Yref)).reshape(M, N)    # stored bf16
     expected = qg.gemm_w4a16(p, X).float().cpu().numpy()   # workspace entry point
     desc = p.desc()
-    if fmt == "int4" and 16 < M < 32 and M % 16:
-        # below M = 32 INT4 runs the same decode kernel on both entry points:
-        # the scratch reserved covers the tail block's plan as well as the
-        # first block's
+    if M > 16 and M % 16 and qg.launch_count(p, M)[1] in ("k_gemv", "k_gemv_tma"):
+        # both entry points run the decode kernel in 16-row blocks: the
+        # scratch reserved covers the tail block's plan as well as the first
+        # block's
         need = lib.qgemm_workspace_size(C.byref(desc), M)
         assert need >= lib.qgemm_workspace_size(C.byref(desc), 16)
         assert need >= lib.qgemm_workspace_size(C.byref(desc), M % 16)
