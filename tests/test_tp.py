@@ -176,10 +176,13 @@ def test_tp_gemm_two_gpus_matches_oracle(O, orc):
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
     world = 2
-    # decode (TMA and LDG-fed), stream-K tcgen05, and block-scaled tcgen05 with
-    # split tiles (its fixup kernel stores the slices and runs the exchange)
+    # decode (TMA and LDG-fed), stream-K tcgen05 (also at M = 20, X padded to
+    # 32 rows), block-scaled tcgen05 with split tiles (its fixup kernel stores
+    # the slices and runs the exchange), and INT4 on the tile tcgen05 kernel
+    # (slice computed, then gathered)
     cases = [("mxfp4", 1024, 1024, 1), ("mxfp4", 2048, 4096, 8), ("nvfp4", 768, 1024, 40), ("int4", 512, 1024, 5),
-             ("mxfp4", 1024, 512, 70), ("mxfp4", 2048, 8192, 32)]
+             ("mxfp4", 1024, 512, 70), ("mxfp4", 2048, 8192, 32), ("nvfp4", 1024, 1024, 20),
+             ("int4", 512, 1024, 24), ("int4", 1024, 2048, 64)]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
