@@ -654,8 +654,8 @@ static size_t decode_tma_workspace(const qgemm_weights_t* w, int sms) { return g
 
 // The tcgen05 paths (dequantised W in TMEM) take M >= 32, and NVFP4 / INT4
 // from M = 17 (one pass over W instead of two 16-row decode passes; X is
-// padded to 32 zero rows): MXFP4 / NVFP4 on the persistent stream-K kernel
-// for M < 128 and K % 256 == 0 (umma_sk.cu), every format on the
+// padded to 32 zero rows): every format on the persistent stream-K kernel
+// for M < 128, K % 256 == 0 and at least 2^26 weights (umma_sk.cu), and on the
 // tile-per-CTA kernel with K splits otherwise (K % 64 == 0, umma.cu).  Their
 // workspace holds the f16 copy of X, its row factors and the split tiles'
 // tickets and partial sums.
@@ -721,14 +721,14 @@ qgemm_status_t gemm_decode_ex(const qgemm_weights_t* w, const uint16_t* X, int M
     float* xs = reinterpret_cast<float*>(head);
     __half* xh = reinterpret_cast<__half*>(head + pad256((size_t)M * sizeof(float)));
     void* part = head + pad256((size_t)M * sizeof(float)) + umma_xh_bytes(w, M);
+    // INT4: X in the pair order int4x8_to_f16 widens codes in
+    const int perm = (w->format == QGEMM_FMT_INT4_G128 || w->format == QGEMM_FMT_INT4_G64) ? 1 : 0;
     if (umma_sk_supported(w, M)) {
       const int bn = umma_sk_bn(M);
-      QG_CUDA_RET(launch_xprep(X, M, (M + bn - 1) / bn * bn, (int)w->K, 0, 1, bn, xh, xs, s));
+      QG_CUDA_RET(launch_xprep(X, M, (M + bn - 1) / bn * bn, (int)w->K, perm, 1, bn, xh, xs, s));
       return gemm_umma_sk(w, xh, xs, M, Y, f32, tickets, part, sm_count_or_zero(), s, tp);
     }
     if (tp) return fail(QGEMM_ERR_UNSUPPORTED_SHAPE, "gemm: no tensor-parallel output on this path");
-    // INT4: X in the pair order int4x8_to_f16 widens codes in
-    const int perm = (w->format == QGEMM_FMT_INT4_G128 || w->format == QGEMM_FMT_INT4_G64) ? 1 : 0;
     QG_CUDA_RET(launch_xprep(X, M, umma_ts_rows(M), (int)w->K, perm, 0, 0, xh, xs, s));
     return gemm_umma_ts(w, xh, xs, M, Y, f32, umma_split_count(w, M), tickets, part, s);
   }

@@ -1,5 +1,6 @@
 // umma_sk.cu -- persistent stream-K tcgen05 W4A16 GEMM for 32 <= M < 128
-// (MXFP4 / NVFP4, K % 256 == 0).
+// (MXFP4; NVFP4 and INT4 g128 / g64 from M = 17; K % 256 == 0; weights of
+// at least 2^26 codes).
 //
 // Y[M,N] = X[M,K] . W[N,K]^T with W in the reference's packed layouts
 // (titoatwork/qgemm-mx include/qgemm/pack.hpp:14-85); X arrives as the f16
@@ -18,6 +19,12 @@
 //          <= 2^13 and e2m1 * factor <= 49152 fits f16; products are exact
 //          while e8m0 >= max - 36 and blocks further down are flushed to
 //          zero.  The epilogue multiplies row n by 2^b.
+//   INT4   q (exact in f16) times the FP16 group scale, rounded to f16
+//          (exact while q s needs at most 11 significant bits); rows whose
+//          largest scale field e over the segment could overflow f16 are
+//          folded by 2^-b, b = max(0, e - 26), multiplied back in the
+//          epilogue.  Codes widen in (c_i, c_i+4) pairs, the order of X from
+//          k_xprep with the INT4 pair permutation.
 //
 // Schedule: one CTA per SM, stream-K.  The iteration space (tile, 256-k step)
 // is cut into one contiguous range per CTA; a CTA walks its range as
@@ -82,7 +89,7 @@ constexpr int kSkThreads = 32 * (kSkEpiWarp0 + kSkEpiWarps);  // 768
 template <int BN>
 struct SkCfg {
   static constexpr int W_CODES = kSkRows * kSkBK / 2;    // 16 KB packed codes
-  static constexpr int W_SCALE_ROW = 16;                 // scale bytes per row per step (MXFP4 8, NVFP4 16)
+  static constexpr int W_SCALE_ROW = 16;                 // scale bytes per row per step (at most 16)
   static constexpr int W_STAGE = W_CODES + kSkRows * W_SCALE_ROW;
   static constexpr int XBOX = BN * 128;                  // 64 k of X (f16), one swizzle row per activation row
   static constexpr int X_STAGE = 4 * XBOX;
@@ -95,6 +102,9 @@ struct SkCfg {
   static_assert(2 * BN + 128 * AST <= 512, "TMEM columns");
   static_assert(SW % kSkWProds == 0, "each W producer owns whole stages");
 };
+
+// scale bytes per weight row per 256-k step: E8M0 / 32, E4M3 / 16, FP16 / 128, FP16 / 64
+constexpr int sk_scale_bytes(int fmt) { return fmt == 0 ? 8 : fmt == 1 ? 16 : fmt == 2 ? 4 : 8; }
 
 struct SkArgs {
   const uint8_t* scales;
@@ -137,6 +147,29 @@ __device__ __forceinline__ int e8m0_row_max(const uint8_t* p, int nbytes) {
   m4 = __vmaxu4(m4, m4 >> 16);
   m4 = __vmaxu4(m4, m4 >> 8);
   return (int)(m4 & 0xFFu);
+}
+
+// Largest exponent field among the FP16 scales in nbytes bytes at p, with
+// infinity / NaN fields (31) counted as 0.  p is 4-byte aligned and nbytes a
+// multiple of 4.
+__device__ __forceinline__ int f16_row_emax(const uint8_t* p, int nbytes) {
+  uint32_t m2 = 0;  // two 16-bit lanes, each the largest field seen there
+  auto fold = [&](uint32_t v) {
+    uint32_t e = (v >> 10) & 0x001F001Fu;
+    e &= ~__vcmpeq2(e, 0x001F001Fu);
+    m2 = __vmaxu2(m2, e);
+  };
+  int i = 0;
+  while (i < nbytes && (reinterpret_cast<uintptr_t>(p + i) & 15u)) {
+    fold(__ldg(reinterpret_cast<const uint32_t*>(p + i)));
+    i += 4;
+  }
+  for (; i + 16 <= nbytes; i += 16) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(p + i));
+    fold(v.x); fold(v.y); fold(v.z); fold(v.w);
+  }
+  for (; i < nbytes; i += 4) fold(__ldg(reinterpret_cast<const uint32_t*>(p + i)));
+  return (int)max(m2 & 0xFFFFu, m2 >> 16);
 }
 
 template <int FMT, int BN, bool F32OUT>
@@ -229,9 +262,9 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
     // mbarrier when their copies land.
     {
       const int p = warp - kSkWProd0;
-      constexpr int SBY = (FMT == 0) ? kSkBK / 32 : kSkBK / 16;  // scale bytes per row per step
+      constexpr int SBY = sk_scale_bytes(FMT);  // scale bytes per row per step
       constexpr int WPR = SBY / 4;
-      const size_t srow = (size_t)a.K / (FMT == 0 ? 32 : 16);
+      const size_t srow = (size_t)a.K / kSkBK * SBY;
       int tile = (int)((it0 + p) / KS), ks = (int)((it0 + p) % KS);
       for (int i = p; i < niter; i += kSkWProds) {
         const int s = i % SW;
@@ -316,8 +349,10 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
     // SWIZZLE_128B: 16-byte chunk c of 128-byte row r sits at chunk c ^ (r % 8)
     const uint32_t w_c0 = (uint32_t)(r * 128 + (((2 * j) ^ (r & 7)) << 4));
     const uint32_t w_c1 = (uint32_t)(r * 128 + (((2 * j + 1) ^ (r & 7)) << 4));
-    // this thread's scale bits in a W stage: MXFP4 two E8M0 bytes, NVFP4 four E4M3 bytes
-    const uint32_t sc_off = (uint32_t)(C::W_CODES + r * C::W_SCALE_ROW + (FMT == 0 ? 2 * j : 4 * j));
+    // this thread's scale bits in a W stage: MXFP4 two E8M0 bytes, NVFP4 four
+    // E4M3 bytes, INT4 one FP16 group scale (g128: group j / 2, g64: group j)
+    const uint32_t sc_off = (uint32_t)(C::W_CODES + r * C::W_SCALE_ROW +
+                                       (FMT == 0 ? 2 * j : FMT == 1 ? 4 * j : FMT == 2 ? 2 * (j >> 1) : 2 * j));
     // W ring position of the next step to load, and of the step being widened
     int ld_s = 0, cur_s = 0;
     uint32_t ld_ph = 0;
@@ -330,16 +365,27 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
       const uint8_t* st = gbase + W_off(stage);
       c0 = *reinterpret_cast<const uint4*>(st + w_c0);
       c1 = *reinterpret_cast<const uint4*>(st + w_c1);
-      sc = (FMT == 0) ? (uint32_t)*reinterpret_cast<const uint16_t*>(st + sc_off)
+      sc = (FMT != 1) ? (uint32_t)*reinterpret_cast<const uint16_t*>(st + sc_off)
                       : *reinterpret_cast<const uint32_t*>(st + sc_off);
       return true;
     };
     // 32 codes -> 16 f16x2 words with their block factors applied
     auto widen = [&](uint4 pk4, uint32_t f_lo, uint32_t f_hi, uint32_t* o) {
-      e2m1x8_to_f16x2(pk4.x, o);
-      e2m1x8_to_f16x2(pk4.y, o + 4);
-      e2m1x8_to_f16x2(pk4.z, o + 8);
-      e2m1x8_to_f16x2(pk4.w, o + 12);
+      if constexpr (FMT >= 2) {
+        const uint32_t qw[4] = {pk4.x, pk4.y, pk4.z, pk4.w};
+#pragma unroll
+        for (int w4 = 0; w4 < 4; ++w4) {
+          uint32_t t[4];
+          int4x8_to_f16(qw[w4], t);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) o[4 * w4 + u] = t[u];
+        }
+      } else {
+        e2m1x8_to_f16x2(pk4.x, o);
+        e2m1x8_to_f16x2(pk4.y, o + 4);
+        e2m1x8_to_f16x2(pk4.z, o + 8);
+        e2m1x8_to_f16x2(pk4.w, o + 12);
+      }
 #pragma unroll
       for (int u = 0; u < 16; ++u) o[u] = hmul2_f16x2(o[u], u < 8 ? f_lo : f_hi);
     };
@@ -355,7 +401,7 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
     for (int i = 0; i < niter && ok; ++i) {
       const bool first = (i == 0) || (kt == 0);
       if (first && i > 0) ++seg;
-      if (FMT == 0 && first) {
+      if (FMT != 1 && first) {
         const int b = seg & 1;
         ok = mbar_wait_flag(basef_bar(b), (seg >> 1) & 1, fault);
         ok = __all_sync(0xFFFFFFFFu, ok);
@@ -379,6 +425,9 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
           f0 = f1 = (b0 == 0xFF) ? 0x7E007E00u : f16x2_pow2(e0);
           f2 = f3 = (b1 == 0xFF) ? 0x7E007E00u : f16x2_pow2(e1);
         }
+      } else if (FMT >= 2) {
+        // FP16 group scale times 2^-rb (rb <= 4: a normal f16)
+        f0 = f1 = f2 = f3 = hmul2_f16x2((sc & 0xFFFFu) | (sc << 16), f16x2_pow2(-rb));
       } else {
         // normal E4M3 codes in one step; zero / subnormal / NaN codes exactly
         uint32_t l0, h0, l1, h1;
@@ -417,7 +466,7 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
     const int r = 32 * q + lane;
     const uint32_t t_lane = (uint32_t)(32 * q) << 16;
     const int first_tile = (int)(it0 / KS);
-    // row factor exponent of a segment (MXFP4), or an L2 prefetch of its scales (NVFP4)
+    // row factor exponent of a segment (MXFP4, INT4), or an L2 prefetch of its scales (NVFP4)
     auto prepare = [&](long long it) -> int {
       const int t = (int)(it / KS), kb = (int)(it % KS);
       const int ke = (int)((kb + (it1 - it)) < KS ? (kb + (it1 - it)) : KS);
@@ -427,6 +476,11 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
         const int m = e8m0_row_max(a.scales + (size_t)n * (a.K / 32) + (size_t)kb * (kSkBK / 32),
                                    (ke - kb) * (kSkBK / 32));
         return m - 127 - 13;
+      }
+      if (FMT >= 2) {
+        constexpr int SBY = sk_scale_bytes(FMT);
+        const int e = f16_row_emax(a.scales + (size_t)n * (a.K / kSkBK * SBY) + (size_t)kb * SBY, (ke - kb) * SBY);
+        return e > 26 ? e - 26 : 0;
       }
       const uint8_t* p = a.scales + (size_t)n * (a.K / 16) + (size_t)kb * (kSkBK / 16);
       for (int off = 0; off < (ke - kb) * (kSkBK / 16); off += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(p + off));
@@ -440,7 +494,7 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
     int rb_cur = 0;
     if (niter > 0) {
       rb_cur = prepare(it0);
-      if (FMT == 0) publish(0, rb_cur);
+      if (FMT != 1) publish(0, rb_cur);
     }
     asm volatile("griddepcontrol.wait;" ::: "memory");  // xs written by the X-preparation grid
     long long it = it0;
@@ -451,9 +505,9 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
       int rb_next = 0;
       if (it_next < it1) {  // next segment's row bases while this one computes
         const int b2 = (seg + 1) & 1;
-        if (FMT == 0 && seg + 1 >= 2) ok = ok && mbar_wait_flag(basee_bar(b2), (((seg + 1) >> 1) + 1) & 1, fault);
+        if (FMT != 1 && seg + 1 >= 2) ok = ok && mbar_wait_flag(basee_bar(b2), (((seg + 1) >> 1) + 1) & 1, fault);
         rb_next = prepare(it_next);
-        if (FMT == 0) publish(b2, rb_next);
+        if (FMT != 1) publish(b2, rb_next);
       }
       const int b = seg & 1;
       ok = ok && mbar_wait_flag(accf_bar(b), (seg >> 1) & 1, fault);
@@ -461,7 +515,7 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
       tc_fence_after();
       const int n = (tile % a.tiles_n) * kSkRows + r, m0 = (tile / a.tiles_n) * BN;
       const bool live = n < a.N;
-      const float rowf = (FMT == 0) ? ldexpf(1.0f, rb_cur) : a.ts;
+      const float rowf = (FMT != 1) ? ldexpf(1.0f, rb_cur) : a.ts;
       const bool whole = (kb == 0 && ke == KS);
       const uint32_t tacc = tmem + t_lane + (uint32_t)(b * BN);
       const int slot = 2 * (int)blockIdx.x + (tile == first_tile ? 0 : 1);
@@ -512,17 +566,31 @@ k_umma_sk(const __grid_constant__ CUtensorMap map_w, const SkArgs a) {
             float acc[16];
 #pragma unroll
             for (int u = 0; u < 16; ++u) acc[u] = 0.0f;
-#pragma unroll 1
-            for (int cc = c_lo; cc <= c_hi; ++cc) {
+            // two contributors' loads in flight, added in CTA order
+            auto src_of = [&](int cc) {
               const int cs = 2 * cc + (tile == (int)(((long long)cc * a.T / a.G) / KS) ? 0 : 1);
-              const float4* src = reinterpret_cast<const float4*>(a.partials + (size_t)cs * (kSkRows * BN) +
-                                                                  (size_t)r * BN + c0);
-              float4 pv[4];
+              return reinterpret_cast<const float4*>(a.partials + (size_t)cs * (kSkRows * BN) + (size_t)r * BN + c0);
+            };
+#pragma unroll 1
+            for (int cc = c_lo; cc <= c_hi; cc += 2) {
+              const bool two = cc < c_hi;
+              const float4* s0 = src_of(cc);
+              const float4* s1 = two ? src_of(cc + 1) : s0;
+              float4 pv[8];
 #pragma unroll
-              for (int u = 0; u < 4; ++u) pv[u] = __ldcg(src + u);
+              for (int u = 0; u < 4; ++u) pv[u] = __ldcg(s0 + u);
+#pragma unroll
+              for (int u = 0; u < 4; ++u) pv[4 + u] = __ldcg(s1 + u);
 #pragma unroll
               for (int u = 0; u < 4; ++u) {
                 acc[4 * u] += pv[u].x; acc[4 * u + 1] += pv[u].y; acc[4 * u + 2] += pv[u].z; acc[4 * u + 3] += pv[u].w;
+              }
+              if (two) {
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                  acc[4 * u] += pv[4 + u].x; acc[4 * u + 1] += pv[4 + u].y; acc[4 * u + 2] += pv[4 + u].z;
+                  acc[4 * u + 3] += pv[4 + u].w;
+                }
               }
             }
             if (live) {
@@ -571,9 +639,19 @@ bool make_tma_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* ptr, 
 
 int umma_sk_bn(int M) { return M >= 64 ? 64 : 32; }
 
+// Weights of at least 2^26 codes (32 MiB packed).  Below that the tile
+// kernel with K splits was as fast or faster (one B200, NVFP4 / INT4 g128,
+// M = 20 / 32 / 64 / 100, CUDA-graph replays of weight-rotated calls):
+// 4096 x 4096 18-24 us against 23-51 us here, 14336 x 4096 and 4096 x 14336
+// within +-8 % except M = 64 (31-39 us against 39-51 us); from 10240 x 8192
+// up this kernel wins (1.1-1.5x; 57344 x 8192 1.5-1.8x), M = 64 at
+// 10240 x 8192 excepted (0.86-0.93x).
+constexpr size_t kSkMinCodes = (size_t)1 << 26;
+
 bool umma_sk_supported(const qgemm_weights_t* w, int M) {
-  return (M >= 32 || (M >= 17 && w->format == QGEMM_FMT_NVFP4)) && M < 128 &&
-         (w->format == QGEMM_FMT_MXFP4 || w->format == QGEMM_FMT_NVFP4) &&
+  return (M >= 32 || (M >= 17 && w->format != QGEMM_FMT_MXFP4)) && M < 128 && w->N * w->K >= kSkMinCodes &&
+         (w->format == QGEMM_FMT_MXFP4 || w->format == QGEMM_FMT_NVFP4 || w->format == QGEMM_FMT_INT4_G128 ||
+          w->format == QGEMM_FMT_INT4_G64) &&
          w->K % kSkBK == 0 && w->K <= (size_t)INT32_MAX && w->N <= (size_t)INT32_MAX &&
          (reinterpret_cast<uintptr_t>(w->scales) & 3u) == 0;
 }
@@ -662,10 +740,20 @@ qgemm_status_t gemm_umma_sk(const qgemm_weights_t* w, const __half* Xh, const fl
     a.tp = *tp;
   }
   cudaError_t e;
-  if (w->format == QGEMM_FMT_MXFP4)
-    e = f32 ? launch_sk_bn<0, true>(p.bn, mw, a, s) : launch_sk_bn<0, false>(p.bn, mw, a, s);
-  else
-    e = f32 ? launch_sk_bn<1, true>(p.bn, mw, a, s) : launch_sk_bn<1, false>(p.bn, mw, a, s);
+  switch (w->format) {
+    case QGEMM_FMT_MXFP4:
+      e = f32 ? launch_sk_bn<0, true>(p.bn, mw, a, s) : launch_sk_bn<0, false>(p.bn, mw, a, s);
+      break;
+    case QGEMM_FMT_NVFP4:
+      e = f32 ? launch_sk_bn<1, true>(p.bn, mw, a, s) : launch_sk_bn<1, false>(p.bn, mw, a, s);
+      break;
+    case QGEMM_FMT_INT4_G128:
+      e = f32 ? launch_sk_bn<2, true>(p.bn, mw, a, s) : launch_sk_bn<2, false>(p.bn, mw, a, s);
+      break;
+    default:
+      e = f32 ? launch_sk_bn<3, true>(p.bn, mw, a, s) : launch_sk_bn<3, false>(p.bn, mw, a, s);
+      break;
+  }
   if (e != cudaSuccess) return fail(QGEMM_ERR_CUDA, "stream-K tcgen05 launch: %s", cudaGetErrorString(e));
   return QGEMM_OK;
 }

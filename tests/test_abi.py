@@ -179,8 +179,15 @@ def test_launch_count_mirrors_dispatch(qg):
     assert count(qg.NVFP4, 8192, 8192, 1, scales=0x1002) == (2, "k_gemv")  # scales not 4-byte aligned
     assert count(qg.INT4_G128, 8192, 8192, 1) == (2, "k_gemv_tma")
     assert count(qg.INT4_G64, 8192, 8192, 16) == (2, "k_gemv_tma")
-    assert count(qg.INT4_G64, 8192, 8192, 20) == (2, "k_umma_ts")            # M >= 17: tcgen05
-    assert count(qg.INT4_G64, 8192, 8192, 64) == (2, "k_umma_ts")
+    assert count(qg.INT4_G64, 8192, 8192, 20) == (2, "k_umma_sk")            # M >= 17: tcgen05
+    assert count(qg.INT4_G128, 8192, 8192, 17) == (2, "k_umma_sk")
+    assert count(qg.INT4_G64, 8192, 8192, 64) == (2, "k_umma_sk")
+    assert count(qg.INT4_G128, 8192, 8192, 127) == (2, "k_umma_sk")
+    assert count(qg.INT4_G128, 8192, 8192, 128) == (2, "k_umma_ts")
+    assert count(qg.INT4_G128, 8192, 8064, 24) == (2, "k_umma_ts")           # K % 256 != 0
+    assert count(qg.INT4_G128, 4096, 8192, 24) == (2, "k_umma_ts")           # below 2^26 weights
+    assert count(qg.NVFP4, 8192, 8192, 40) == (2, "k_umma_sk")           # 2^26 weights
+    assert count(qg.NVFP4, 8191, 8192, 40) == (2, "k_umma_ts")
     assert count(qg.INT4_G128, 8192, 8192, 2048) == (2, "k_umma_ts")
     assert count(qg.INT4_G128, 8192, 8064, 1) == (2, "k_gemv")              # K % 256 != 0: LDG-fed
     assert count(qg.INT4_G64, 8192, 8192, 1, scales=0x1004) == (2, "k_gemv")  # scales not 8-byte aligned

@@ -9,6 +9,8 @@ titoatwork/qgemm-mx include/qgemm/ref_gemm.hpp:15-27), through the C-ABI:
   M range (TMA decode for M <= 8, block-scaled tcgen05 for M = 32, 64);
 * the 8B-class MXFP4 layer set at the M values no other test covers, the
   O projection 4096x4096 included;
+* NVFP4 and INT4 layers of 2^26 weights or more at 17 <= M < 128 (the
+  stream-K tcgen05 kernel), INT4 rows with scales that need folding among them;
 * compute-bound prefill, NVFP4 (28672, 8192) and (8192, 28672) at M = 2048;
 * exact probes (one nonzero weight per row, random codes with prime / narrow
   scales, sparse power-of-two activations): every product and partial sum is
@@ -64,7 +66,8 @@ def _host_bytes(fmt, p):
     return u8(p.data), (u16(p.scales) if fmt == "int4" else u8(p.scales))
 
 
-def _sampled_blocks(qg, orc, O, fmt, group, p, d, s, M, seed, nblocks=4, expect_kernel=None):
+def _sampled_blocks(qg, orc, O, fmt, group, p, d, s, M, seed, nblocks=4, expect_kernel=None, rel_f32=1e-5,
+                    frob_bf16=1e-3):
     N, K = p.N, p.K
     if expect_kernel:
         assert qg.launch_count(p, M)[1] == expect_kernel, (M, qg.launch_count(p, M))
@@ -79,9 +82,9 @@ def _sampled_blocks(qg, orc, O, fmt, group, p, d, s, M, seed, nblocks=4, expect_
                        n_end=n0 + 64, nthreads=16, Y=Yref)
         ref = Yref[:, n0:n0 + 64]
         ok, ratio, rel = within_tolerance(Yf[:, n0:n0 + 64], ref)
-        assert ok and rel < 1e-5, ("f32", M, n0, ratio, rel)
+        assert ok and rel < rel_f32, ("f32", M, n0, ratio, rel)
         refb = O.bf16_bits_to_f32(O.f32_to_bf16_bits(ref)).reshape(ref.shape)
-        ok, ratio, rel = within_tolerance(Yb[:, n0:n0 + 64], refb)
+        ok, ratio, rel = within_tolerance(Yb[:, n0:n0 + 64], refb, frob_tol=frob_bf16)
         assert ok, ("bf16", M, n0, ratio, rel)
 
 
@@ -119,6 +122,51 @@ def test_8b_layer_set_sweep(qg, cuda, O, orc, name, N, K, ms):
     d, s = _host_bytes("mxfp4", p)
     for M in ms:
         _sampled_blocks(qg, orc, O, "mxfp4", 32, p, d, s, M, seed=M + 3, nblocks=3)
+
+
+# ---- NVFP4 / INT4 layers of 2^26 weights and more at 17 <= M < 128 ----------------------
+# The stream-K tcgen05 kernel: tiles split across CTAs and summed by the last
+# arriver, per-segment INT4 row folds; M = 17 and 20 pad X to 32 rows.  INT4
+# enters the tensor core as q x scale rounded to f16 (relative Frobenius
+# bound 1e-3 on the FP32 output, as for the tile kernel).
+
+CFG_SK = [
+    ("nvfp4", 16, 10240, 8192, [17, 40, 64, 100]),
+    ("int4", 128, 10240, 8192, [20, 32, 64, 127]),
+    ("int4", 64, 8192, 28672, [24, 96]),
+]
+
+
+@pytest.mark.parametrize("fmt,group,N,K,ms", CFG_SK)
+def test_stream_k_layers(qg, cuda, O, orc, fmt, group, N, K, ms):
+    W, p = _dev_pack(qg, fmt, group, N, K, seed=N + 3 * K + group)
+    _check_packed_rows(orc, fmt, group, W, p, [16, N - 16])
+    del W
+    d, s = _host_bytes(fmt, p)
+    for M in ms:
+        _sampled_blocks(qg, orc, O, fmt, group, p, d, s, M, seed=M + 5, nblocks=3, expect_kernel="k_umma_sk",
+                        rel_f32=1e-3 if fmt == "int4" else 1e-5)
+
+
+def test_stream_k_int4_large_scales(qg, cuda, O, orc):
+    """Every fourth row's FP16 group scales near 2^14 (|W| ~ 1e5): the
+    stream-K kernel folds those rows by a power of two per segment and
+    multiplies it back in the epilogue.  The bf16 output is held to 2e-3
+    relative Frobenius: the FP32 result's error from q x scale rounded to f16
+    (below 1e-3) flips the bf16 rounding of some outputs by one unit (2^-8
+    relative), which the columns of the large rows carry."""
+    N, K = 8192, 8192
+    g = torch.Generator(device="cuda")
+    g.manual_seed(29)
+    W = torch.randn((N, K), generator=g, device="cuda", dtype=torch.float32) * 0.02
+    W[::4] *= 2e6  # group scales ~1.5e4, the largest below f16's 65504
+    p = qg.pack_int4(W, 128)
+    del W
+    d, s = _host_bytes("int4", p)
+    assert int(s.max() >> 10 & 0x1F) > 26  # the folded case is reached
+    for M in (24, 64):
+        _sampled_blocks(qg, orc, O, "int4", 128, p, d, s, M, seed=M + 7, nblocks=3, expect_kernel="k_umma_sk",
+                        rel_f32=1e-3, frob_bf16=2e-3)
 
 
 # ---- compute-bound prefill (NVFP4, M = 2048) ------------------------------------------

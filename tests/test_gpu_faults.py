@@ -36,10 +36,12 @@ def _packed(qg, O, fmt, group, N, K, seed=0):
 
 
 WS_CASES = [  # (format, group, N, K, M values): one per dispatch path, and INT4 tails
-    ("int4", 128, 14336, 4096, [16, 17, 18, 20, 24, 40]),  # TMA decode, then the tile tcgen05 kernel
+    ("int4", 128, 14336, 4096, [16, 17, 18, 20, 24, 40, 130]),  # TMA decode, then the tile tcgen05 kernel
     ("int4", 64, 4096, 4096, [1, 16, 33]),
+    ("int4", 64, 8192, 8192, [24, 100]),                # stream-K tcgen05 (2^26 weights)
     ("mxfp4", 32, 4096, 4096, [1, 8, 16, 64]),          # TMA decode, block-scaled
-    ("nvfp4", 16, 4096, 4096, [1, 16, 40, 130]),        # TMA decode, stream-K and tile tcgen05
+    ("nvfp4", 16, 4096, 4096, [1, 16, 40, 130]),        # TMA decode, tile tcgen05
+    ("nvfp4", 16, 8192, 8192, [20, 64]),                # stream-K tcgen05
     ("mxfp4", 32, 2880, 2880, [1, 40, 200]),            # LDG decode (K % 256 != 0), tile tcgen05
 ]
 

@@ -93,12 +93,14 @@ def test_gemm_split_k_tcgen05(qg, cuda, O, orc, fmt, group, M):
 
 
 @pytest.mark.parametrize("group", [128, 64])
-@pytest.mark.parametrize("M", [32, 64, 200])
-def test_gemm_int4_tcgen05(qg, cuda, O, orc, group, M):
-    """INT4 from M = 32 runs the tile tcgen05 kernel, K split across CTAs:
-    two calls give the same bits, and Y is within the contract's tolerance
-    (W enters the tensor core as q x scale rounded to f16)."""
-    N, K = 300, 8192
+@pytest.mark.parametrize("M,K", [(20, 8192), (32, 8192), (64, 8192), (127, 4096), (200, 8192), (40, 8064)])
+def test_gemm_int4_tcgen05(qg, cuda, O, orc, group, M, K):
+    """INT4 from M = 17 on weights below 2^26 codes runs the tile tcgen05
+    kernel, K split across CTAs (the stream-K kernel takes larger weights,
+    covered with the layer shapes): two calls give the same bits, and Y is
+    within the contract's tolerance (W enters the tensor core as q x scale
+    rounded to f16)."""
+    N = 300
     p, d, s, ts = packed_pair(qg, O, orc, "int4", group, N, K, seed=M + group)
     assert qg.launch_count(p, M)[1] == "k_umma_ts"
     X = O.randn_bf16(M, 2, M * K).reshape(M, K)
@@ -112,19 +114,23 @@ def test_gemm_int4_tcgen05(qg, cuda, O, orc, group, M):
     assert ok and rel < 1e-3, (ratio, rel)
 
 
-def test_gemm_int4_tcgen05_large_scales(qg, cuda, O, orc):
+@pytest.mark.parametrize("group,K", [(128, 1024), (64, 1088)])
+def test_gemm_int4_tcgen05_large_scales(qg, cuda, O, orc, group, K):
     """INT4 rows with FP16 group scales near 2^14 (|W| ~ 1e5) next to ordinary
-    rows: q x scale would leave f16's range, so the kernel folds those rows
-    by a power of two and multiplies it back in the epilogue."""
-    N, K, M = 256, 1024, 64
+    rows: q x scale would leave f16's range, so the tile tcgen05 kernel folds
+    those rows by a power of two and multiplies it back in the epilogue (the
+    stream-K kernel's fold is covered with the layer shapes)."""
+    kernel = "k_umma_ts"
+    N, M = 256, 64
     W = weights(O, N, K, seed=17)
     W[::4] *= 4e6
     Wd = to_dev_f32(W)
-    p = qg.pack_int4(Wd, 128)
+    p = qg.pack_int4(Wd, group)
+    assert qg.launch_count(p, M)[1] == kernel
     d, s = u8(p.data), u16(p.scales)
     assert int(s.max() >> 10 & 0x1F) > 26  # the folded case is reached
     X = O.randn_bf16(9, 2, M * K).reshape(M, K)
-    Yref = orc.w4a16_gemm("int4", d, s, N, K, X, group=128, nthreads=8)
+    Yref = orc.w4a16_gemm("int4", d, s, N, K, X, group=group, nthreads=8)
     Y = run(qg, p, X, f32=True)
     assert np.isfinite(Y).all()
     ok, ratio, rel = within_tolerance(Y, Yref)

@@ -176,13 +176,15 @@ def test_tp_gemm_two_gpus_matches_oracle(O, orc):
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
     world = 2
-    # decode (TMA and LDG-fed), stream-K tcgen05 (also at M = 20, X padded to
-    # 32 rows), block-scaled tcgen05 with split tiles (its fixup kernel stores
-    # the slices and runs the exchange), and INT4 on the tile tcgen05 kernel
-    # (slice computed, then gathered)
+    # decode (TMA and LDG-fed), block-scaled tcgen05 with split tiles (its
+    # fixup kernel stores the slices and runs the exchange), NVFP4 and INT4
+    # on the stream-K tcgen05 kernel (shards of 2^26 weights; M = 20 has X
+    # padded to 32 rows), and NVFP4 / INT4 shards below that size, or with
+    # K % 256 != 0, on the tile tcgen05 kernel (slice computed, then gathered)
     cases = [("mxfp4", 1024, 1024, 1), ("mxfp4", 2048, 4096, 8), ("nvfp4", 768, 1024, 40), ("int4", 512, 1024, 5),
              ("mxfp4", 1024, 512, 70), ("mxfp4", 2048, 8192, 32), ("nvfp4", 1024, 1024, 20),
-             ("int4", 512, 1024, 24), ("int4", 1024, 2048, 64)]
+             ("int4", 512, 1024, 24), ("int4", 1024, 2048, 64), ("int4", 512, 1152, 24),
+             ("nvfp4", 16384, 8192, 20), ("int4", 16384, 8192, 40)]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -207,7 +209,7 @@ def test_tp_gemm_two_gpus_matches_oracle(O, orc):
         ts = O.nvfp4_tensor_scale(W) if fmt == "nvfp4" else 1.0
         for r in range(world):
             st, d, s = orc.pack(fmt, np.ascontiguousarray(W[r * n_loc:(r + 1) * n_loc]), tensor_scale=ts)
-            parts.append(orc.w4a16_gemm(fmt, d, s, n_loc, K, X, tensor_scale=ts))
+            parts.append(orc.w4a16_gemm(fmt, d, s, n_loc, K, X, tensor_scale=ts, nthreads=16))
         Yref = np.concatenate(parts, axis=1)
         Yref = O.bf16_bits_to_f32(O.f32_to_bf16_bits(Yref)).reshape(M, N)  # Y is stored bf16, like the reference
         for r in range(world):
