@@ -1,6 +1,7 @@
 // umma.cu -- tile-per-CTA tcgen05 (5th-generation tensor core) W4A16 GEMM
-// for M >= 128 (and for 32 <= M < 128 when K % 256 != 0, and for INT4 from
-// M = 17).
+// for M >= 128, and below that where the stream-K kernel (umma_sk.cu) does
+// not apply: K % 256 != 0, or weights of fewer than 2^26 codes (NVFP4 and
+// INT4 from M = 17, X padded to 32 rows below M = 32).
 //
 // Y[M,N] = X[M,K] . W[N,K]^T, W packed in the reference layouts
 // (titoatwork/qgemm-mx include/qgemm/pack.hpp:14-85); X arrives as the f16

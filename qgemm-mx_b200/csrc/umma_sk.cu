@@ -57,7 +57,8 @@
 //   warps 20..23  epilogue: drain accumulator buffers (double-buffered, so
 //                 the next segment's MMAs overlap the drain), split-tile
 //                 tickets and reductions; ahead of each segment they compute
-//                 the MXFP4 row bases (or prefetch NVFP4 scales into L2).
+//                 the MXFP4 row bases and INT4 row folds (or prefetch NVFP4
+//                 scales into L2).
 // TMEM: [acc 0 | acc 1 | AST A stages of 128 columns (256 k, f16 pairs)].
 //
 // Every mbarrier wait is bounded (tc.cuh); on timeout the kernel sets
