@@ -6,8 +6,8 @@ f16, after the row was folded by 2^-b, b = max(0, e - 26) with e the largest
 FP16 exponent field among the row's scales; the epilogue multiplies by 2^b.
 X enters as f16 scaled by a power of two per row (exact for bf16 values in
 range), products are exact in the FP32 accumulator, so W's rounding is the
-only difference from the reference's exact q * s (pack.hpp dequant_int4,
-ref_gemm.hpp:15-27) beyond summation order.
+only difference from the reference's exact q * s (dequant_int4,
+pack.hpp:548-604; ref_gemm.hpp:15-27) beyond summation order.
 
 This model, in float64 on the oracle's packed bytes, shows:
 * q * s is exact while it needs at most 11 significant bits (scales of up to
