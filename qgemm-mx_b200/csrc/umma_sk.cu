@@ -105,7 +105,7 @@ struct SkCfg {
 };
 
 // scale bytes per weight row per 256-k step: E8M0 / 32, E4M3 / 16, FP16 / 128, FP16 / 64
-constexpr int sk_scale_bytes(int fmt) { return fmt == 0 ? 8 : fmt == 1 ? 16 : fmt == 2 ? 4 : 8; }
+__host__ __device__ constexpr int sk_scale_bytes(int fmt) { return fmt == 0 ? 8 : fmt == 1 ? 16 : fmt == 2 ? 4 : 8; }
 
 struct SkArgs {
   const uint8_t* scales;
