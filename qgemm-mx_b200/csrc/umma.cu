@@ -65,7 +65,8 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
 //          b_n = max_blocks(e8m0) - 127 - 13, so every factor 2^(t-b_n) <= 2^13
 //          and e2m1 * 2^(t-b_n) <= 49152 fits f16.  Products are exact while
 //          t - b_n >= -23 (a 37-binade window below the row's largest block);
-//          blocks further down are flushed to zero.  The epilogue multiplies
+//          the next binade rounds to f16's smallest subnormals and blocks
+//          below it are flushed to zero.  The epilogue multiplies
 //          row n by 2^b_n and column m by the X prescale 2^s_m.
 //   INT4   q (exact in f16) times the FP16 group scale, rounded to f16
 //          (exact while q s needs <= 11 significant bits, e.g. scales of up

@@ -17,8 +17,9 @@
 //   MXFP4  2^(e8m0-127) is folded relative to a per-row, per-segment base
 //          b = max(e8m0) - 140 over the segment's blocks, so every factor is
 //          <= 2^13 and e2m1 * factor <= 49152 fits f16; products are exact
-//          while e8m0 >= max - 36 and blocks further down are flushed to
-//          zero.  The epilogue multiplies row n by 2^b.
+//          while e8m0 >= max - 36; the next binade rounds to f16's smallest
+//          subnormals and blocks below it are flushed to zero.  The epilogue
+//          multiplies row n by 2^b.
 //   INT4   q (exact in f16) times the FP16 group scale, rounded to f16
 //          (exact while q s needs at most 11 significant bits); rows whose
 //          largest scale field e over the segment could overflow f16 are
@@ -117,7 +118,7 @@ struct SkArgs {
   long long T;          // tiles * KS
   int M, N, K;
   int tiles_n;          // tile t -> rows (t % tiles_n) * 128, activations (t / tiles_n) * BN
-  int KS;               // steps per tile (K / 128)
+  int KS;               // steps per tile (K / 256)
   int G;                // CTAs
   float ts;
   TpOut tp;             // world > 0: store into every rank's Y_full, then tp_finish

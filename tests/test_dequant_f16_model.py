@@ -13,7 +13,8 @@ operands exactly into FP32.  Over every code and scale byte:
   row or segment) - 140, made by f16x2_pow2 (tc.cuh: 2^k for k >= -24, else
   zero), and the epilogue multiplies by 2^b.  Products never exceed 49152
   (no overflow) and are exact for every block within 36 binades of the
-  largest; the first block further down is the first that can round.
+  largest; the next binade rounds to f16's smallest subnormals and blocks
+  below it get a zero factor.
 No GPU is involved; the GPU tests check the kernels against the oracle.
 """
 import numpy as np
@@ -63,3 +64,4 @@ def test_mxfp4_folded_products(orc, mx):
     assert np.all(got[:, near] == exact[:, near]), mx
     if mx >= 37:
         assert np.any(got[:, e == mx - 37] != exact[:, e == mx - 37])  # the band is tight
+        assert not got[:, e < mx - 37].any()                           # zero factor below
