@@ -17,7 +17,9 @@ This model, in float64 on the oracle's packed bytes, shows:
   Frobenius bound the GPU tests hold INT4 on these kernels to, and above the
   1e-5 bound of the other formats (which is why INT4 has its own bound);
 * rows whose scales reach f16's top binades overflow without the fold and
-  stay finite with it.
+  stay finite with it;
+* the bit operations that widen eight INT4 codes to f16 give exact values
+  in the pair order of k_xprep's INT4 permutation of X.
 No GPU is involved: this is the tolerance's derivation, not a parity test.
 """
 import numpy as np
@@ -96,3 +98,33 @@ def test_fold_keeps_large_rows_finite(O, orc):
     Y = X @ w.T
     assert np.isfinite(Y).all()
     assert _rel(Y, Yref) < 1e-3
+
+
+def _halves(w):
+    """The two f16 halves (low, high) of a 32-bit word, as float64."""
+    h = np.array([w & 0xFFFF, w >> 16], np.uint16).view(np.float16)
+    return h.astype(np.float64)
+
+
+def test_int4_widening_pairs_match_the_x_permutation():
+    """int4x8_to_f16 (gemv_core.cuh) restated with its bit operations: one
+    32-bit word of eight two's-complement nibbles c0..c7 (c0 in bits 0-3)
+    becomes four f16 pairs (c0, c4), (c1, c5), (c2, c6), (c3, c7), each value
+    exact, which is the order k_xprep's INT4 permutation gives X
+    (f16 pair i = (x_i, x_{i+4}))."""
+    magic, sub, k16, neg72 = 0x6400, 1032.0, 1.0 / 16.0, -72.0
+    rng = np.random.default_rng(5)
+    words = list(rng.integers(0, 2 ** 32, 2000, dtype=np.uint64)) + [0, 0xFFFFFFFF, 0x88888888, 0x77777777]
+    for q in words:
+        q = int(q)
+        nib = [(q >> (4 * i)) & 0xF for i in range(8)]
+        val = [n - 16 if n >= 8 else n for n in nib]
+        lo = q ^ 0x88888888
+        hi = lo >> 8
+        w0 = (lo & 0x000F000F) | (magic | magic << 16)
+        w1 = (lo & 0x00F000F0) | (magic | magic << 16)
+        w2 = (hi & 0x000F000F) | (magic | magic << 16)
+        w3 = (hi & 0x00F000F0) | (magic | magic << 16)
+        pairs = [_halves(w0) - sub, _halves(w1) * k16 + neg72, _halves(w2) - sub, _halves(w3) * k16 + neg72]
+        for i, p in enumerate(pairs):
+            assert p.tolist() == [val[i], val[i + 4]], (hex(q), i)
