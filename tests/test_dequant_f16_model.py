@@ -5,8 +5,9 @@ f16 (cvt.rn.f16x2.e2m1x2, exact) and multiply by an f16 block factor with one
 f16x2 multiply, rounded to nearest even; the tensor core then multiplies f16
 operands exactly into FP32.  Over every code and scale byte:
 
-* NVFP4: the factor is the E4M3 scale itself, and e2m1 x e4m3 is exact in
-  f16 for every finite pair (the FP32 tensor scale is applied in the
+* NVFP4: the factor is the E4M3 scale itself, decoded by bit placement for
+  normal codes (the exact decoder for the rest), and e2m1 x e4m3 is exact
+  in f16 for every finite pair (the FP32 tensor scale is applied in the
   epilogue), so the kernels see the reference's dequantised values
   (pack.hpp:548-604) exactly.
 * MXFP4: the factor is 2^(e - 127 - b) with b = (largest E8M0 byte of the
@@ -65,3 +66,19 @@ def test_mxfp4_folded_products(orc, mx):
     if mx >= 37:
         assert np.any(got[:, e == mx - 37] != exact[:, e == mx - 37])  # the band is tight
         assert not got[:, e < mx - 37].any()                           # zero factor below
+
+
+def test_e4m3_decode_by_bit_placement(orc):
+    """e4m3x2_to_f16x2_fast (gemv_core.cuh) restated: a normal E4M3 byte's
+    exponent and mantissa bits, shifted into f16 position with the exponent
+    rebased (+8), are the f16 of its value; it declines exactly the zero,
+    subnormal and NaN codes, which the kernels decode with the exact path."""
+    for b in range(256):
+        e, m7 = (b >> 3) & 0xF, b & 0x7F
+        ok = e != 0 and m7 != 0x7F
+        h = ((b & 0x80) << 8) | ((m7 << 7) + 0x2000)
+        ref = orc.e4m3_decode(b)
+        if ok:
+            assert float(np.array([h], np.uint16).view(np.float16)[0]) == ref, b
+        else:
+            assert e == 0 or np.isnan(ref), b
