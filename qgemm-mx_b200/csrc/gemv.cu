@@ -11,7 +11,7 @@
 // Two launches per call, chained with programmatic dependent launch:
 //  k_xprep  X (bf16) -> f16 with a per-row power-of-two prescale 2^-s_m chosen
 //           so that max|x_m| * 2^-s_m lies in [2^14, 2^15).  Every bf16 value
-//           at or above max|x_m| * 2^-29 converts exactly (8 significant bits
+//           at or above max|x_m| * 2^-31 converts exactly (8 significant bits
 //           fit f16's 11); smaller ones round to f16's subnormal grid, an
 //           error below 2^-39 * max|x_m| per element.  The FP32 epilogue
 //           multiplies by 2^s_m, so no information is lost.

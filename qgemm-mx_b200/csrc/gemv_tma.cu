@@ -12,7 +12,7 @@
 // X is prepared once per call by k_xprep_units, one warp per (activation
 // row, 256-k unit): f16 scaled by a power of two 2^-s per row and unit, with
 // the row's largest |x| in the unit in [2^14, 2^15), so every bf16 value at or
-// above 2^-29 of that largest converts exactly (its 8 significant bits fit
+// above 2^-31 of that largest converts exactly (its 8 significant bits fit
 // f16's 11) and smaller ones round to f16's subnormal grid.  The unit's image
 // and its row factors 2^s are one contiguous block the producers bulk-copy
 // beside the weights.  The consumers sum each unit into a partial and add
