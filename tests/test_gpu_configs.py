@@ -202,9 +202,9 @@ def test_prefill_sampled_rows(qg, cuda, O, orc, N, K):
 
 PROBE_FORMATS = [("mxfp4", 32), ("nvfp4", 16), ("int4", 128), ("int4", 64)]
 # M values that route to each kernel: 1 and 8 decode (TMA or LDG), 12 block-scaled
-# (MXFP4) / decode, 40 block-scaled (MXFP4) / stream-K tcgen05 (NVFP4), 130 tile
-# tcgen05 (MXFP4 and NVFP4); INT4: the decode kernel in 16-row blocks below
-# M = 32 (TMA-fed when K % 256 == 0), the tile tcgen05 kernel from M = 32.
+# (MXFP4) / decode, 40 block-scaled (MXFP4) / tile tcgen05 (NVFP4, INT4), 130
+# tile tcgen05 (every format).  The stream-K tcgen05 kernel takes weights of
+# 2^26 codes and more: test_exact_random_codes_stream_k below.
 PROBE_M = [1, 8, 12, 40, 130]
 
 
@@ -248,3 +248,17 @@ def test_exact_one_hot_permutation(qg, cuda, O, orc, fmt, group, M):
     Yref = _exact(qg, O, orc, fmt, group, N, K, d, s, ts, X)
     nz = np.argwhere(Yref != 0)
     assert np.array_equal(nz[:, 1], np.arange(M) % N)
+
+
+@pytest.mark.parametrize("fmt,group", [("nvfp4", 16), ("int4", 128), ("int4", 64)])
+def test_exact_random_codes_stream_k(qg, cuda, O, orc, fmt, group):
+    """The random-code probe on 65536 x 1024 weights (2^26 codes), which
+    route M = 40 to the stream-K tcgen05 kernel.  K as in the probes above
+    keeps every partial sum exact, so the split tiles' partials, parked by
+    several CTAs and summed by the last, must give the oracle's bits."""
+    N, K, M = 65536, 1024, 40
+    d, s, ts = P.random_weights(fmt, group, N, K, seed=M + group)
+    assert qg.launch_count(qg.from_host(_fcode(qg, fmt, group), N, K, d, s, ts), M)[1] == "k_umma_sk"
+    X = P.sparse_activations(M, K, seed=140 + group)
+    Yref = _exact(qg, O, orc, fmt, group, N, K, d, s, ts, X)
+    assert np.count_nonzero(Yref) > Yref.size // 2
